@@ -1,0 +1,159 @@
+/*
+ * moe_b200.h -- C ABI of the B200 (sm_100a) DeepSeek-V3 FP8 block-scale MoE layer.
+ *
+ * The layer is the contest definition
+ * moe_fp8_block_scale_ds_routing_topk8_ng8_kg4_e32_h7168_i2048 of the reference
+ * (spec/definition.json:1-146).  Its Python entry point `run(...)` /
+ * `kernel(...)` (spec/reference_official.py:5-16,
+ * solution/python/kernel.py:1448-1459) is mirrored by moe_swarm_b200.run, which
+ * calls moe_b200_forward below.  The reference's own native boundary was a
+ * pybind11 module exporting gemm1 / gemm1_streaming / gemm2 over raw uintptr_t
+ * pointers and a stream (solution/python/kernel.py:2497-2499, :2543-2551); this
+ * header replaces it with one C entry point for the whole layer plus a
+ * routing-only entry point for tests.
+ *
+ * Conventions: plain pointers to device memory, sizes in elements, the CUDA
+ * stream passed as an opaque pointer (NULL = legacy default stream), integer
+ * status codes (0 = success), no exceptions, no torch types.  All work is
+ * enqueued on the stream without a host synchronisation, so calls can be
+ * captured in a CUDA graph.  Device-side failures (a bounded wait that timed
+ * out) are reported through moe_b200_device_status.
+ */
+#ifndef MOE_B200_H_
+#define MOE_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MOE_B200_API __attribute__((visibility("default")))
+#else
+#define MOE_B200_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Fixed DeepSeek-V3 geometry (spec/definition.json:8-54). */
+#define MOE_B200_HIDDEN 7168
+#define MOE_B200_INTER 2048
+#define MOE_B200_EXPERTS 256
+#define MOE_B200_TOPK 8
+
+/* Status codes. */
+#define MOE_B200_OK 0
+#define MOE_B200_ERR_ARG 1         /* a null pointer, a bad size or an unsupported E_local */
+#define MOE_B200_ERR_WORKSPACE 2   /* workspace too small (see moe_b200_workspace_size) */
+#define MOE_B200_ERR_CUDA 3        /* a CUDA runtime/driver call failed (see moe_b200_last_error) */
+#define MOE_B200_ERR_DEVICE 4      /* an sm_100 device is required */
+#define MOE_B200_ERR_TIMEOUT 5     /* a device-side bounded wait gave up (device status) */
+
+/*
+ * Arguments of one layer call.  Tensor layouts are exactly those of
+ * spec/definition.json:57-145 (all row-major, contiguous):
+ *   routing_logits       f32  [T, 256]
+ *   routing_bias         bf16 [256]                 (raw 16-bit words)
+ *   hidden_states        e4m3 [T, 7168]             (raw bytes)
+ *   hidden_states_scale  f32  [56, T]               (transposed per-token 1x128 scales)
+ *   gemm1_weights        e4m3 [E_local, 4096, 7168]
+ *   gemm1_weights_scale  f32  [E_local, 32, 56]
+ *   gemm2_weights        e4m3 [E_local, 7168, 2048]
+ *   gemm2_weights_scale  f32  [E_local, 56, 16]
+ *   output               bf16 [T, 7168]             (written in full)
+ * E_local may be any value in [1, 256]; the reference fixes it to 32
+ * (spec/reference_official.py:44) and treats other values as expert
+ * parallelism by local_expert_offset (reference/kernel_pytorch_v1.py:126-130).
+ * The weight base pointers must be 16-byte aligned (TMA).
+ */
+typedef struct moe_b200_args {
+  const float* routing_logits;
+  const uint16_t* routing_bias;
+  const uint8_t* hidden_states;
+  const float* hidden_states_scale;
+  const uint8_t* gemm1_weights;
+  const float* gemm1_weights_scale;
+  const uint8_t* gemm2_weights;
+  const float* gemm2_weights_scale;
+  uint16_t* output;
+  int32_t num_tokens;            /* T >= 0 */
+  int32_t num_local_experts;     /* E_local */
+  int32_t local_expert_offset;   /* global id of local expert 0 */
+  float routed_scaling_factor;
+} moe_b200_args;
+
+/*
+ * Byte offsets of the per-call buffers inside a workspace, for tests and
+ * tools that read the routing results back.  Arrays sized by T are laid out
+ * for the T passed to moe_b200_workspace_layout.
+ */
+typedef struct moe_b200_layout {
+  size_t plan;        /* int32[16]: T, E_local, rows, m_tiles, s1, kb1, units1, s2, kb2, units2 */
+  size_t topk_idx;    /* int32 [T, 8]: selected global experts, ascending per token */
+  size_t topk_w;      /* f32   [T, 8]: their combine weights (bias-free, normalised, x rsf) */
+  size_t tok_nloc;    /* int32 [T]: number of local experts each token selected */
+  size_t tok_rows;    /* int32 [T, 8]: permuted row of each local pick, ascending expert */
+  size_t e_count;     /* int32 [E_local]: rows per local expert */
+  size_t e_start;     /* int32 [E_local + 1]: first permuted row of each local expert */
+  size_t row_token;   /* int32 [R]: token of each permuted row (expert-major, token-minor) */
+  size_t row_weight;  /* f32   [R]: combine weight of each permuted row */
+  size_t c_hi;        /* e4m3  [R, 2048]: SwiGLU output, high part */
+  size_t c_lo;        /* e4m3  [R, 2048]: SwiGLU output, residual x16 */
+  size_t c_scale;     /* f32   [16, r_pad]: per-(row, 128-block) scale of c_hi */
+  size_t status;      /* int32: device status word (0 = ok) */
+  size_t r_max;       /* rows reserved: T * min(8, E_local) */
+  size_t r_pad;       /* leading dimension of the [blocks, rows] scale arrays */
+  size_t total;       /* bytes */
+} moe_b200_layout;
+
+/* Workspace bytes one call with this T and E_local needs (0 on bad arguments). */
+MOE_B200_API size_t moe_b200_workspace_size(int32_t num_tokens, int32_t num_local_experts);
+
+/* Fills *out with the layout for (T, E_local).  Returns a status code. */
+MOE_B200_API int moe_b200_workspace_layout(int32_t num_tokens, int32_t num_local_experts,
+                              moe_b200_layout* out);
+
+/*
+ * Zeroes the self-resetting counters and the status word of a freshly
+ * allocated workspace.  Call once after allocating (or after a call that
+ * returned an error); later calls leave the counters zeroed themselves.
+ */
+MOE_B200_API int moe_b200_workspace_init(void* workspace, size_t workspace_bytes, int32_t num_tokens,
+                            int32_t num_local_experts, void* stream);
+
+/*
+ * One MoE layer call: routing, permutation, GEMM1 + SwiGLU, GEMM2 + weighted
+ * combine, bf16 output.  Replaces the whole of kernel(...)
+ * (solution/python/kernel.py:1448-1538) and run(...)
+ * (spec/reference_official.py:5-168).
+ */
+MOE_B200_API int moe_b200_forward(const moe_b200_args* args, void* workspace, size_t workspace_bytes,
+                     void* stream);
+
+/*
+ * Routing and permutation only (the reference's _route_kernel + _pf_permute_kernel,
+ * solution/python/kernel.py:137-213, :1211-1243): fills the routing arrays of the
+ * layout and zeroes output rows of tokens with no local expert.
+ */
+MOE_B200_API int moe_b200_route(const moe_b200_args* args, void* workspace, size_t workspace_bytes,
+                   void* stream);
+
+/*
+ * Synchronises the stream and returns the device status word (0 = ok,
+ * otherwise the code of the first bounded wait that timed out); with
+ * `clear` != 0 the word is reset.
+ */
+MOE_B200_API int moe_b200_device_status(void* workspace, size_t workspace_bytes, int32_t num_tokens,
+                           int32_t num_local_experts, void* stream, int32_t clear);
+
+/* Text of the last host-side error of this thread ("" if none). */
+MOE_B200_API const char* moe_b200_last_error(void);
+
+/* Number of kernels the last moe_b200_forward call on this thread enqueued. */
+MOE_B200_API int moe_b200_last_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOE_B200_H_ */

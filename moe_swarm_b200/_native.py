@@ -1,0 +1,99 @@
+"""ctypes binding of libmoe_b200.so (the C ABI declared in include/moe_b200.h).
+
+Loading fails loudly when the library has not been built: there is no fallback.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().with_name("libmoe_b200.so")
+
+OK = 0
+ERR_ARG = 1
+ERR_WORKSPACE = 2
+ERR_CUDA = 3
+ERR_DEVICE = 4
+ERR_TIMEOUT = 5
+
+EXPORTED = (
+    "moe_b200_workspace_size",
+    "moe_b200_workspace_layout",
+    "moe_b200_workspace_init",
+    "moe_b200_forward",
+    "moe_b200_route",
+    "moe_b200_device_status",
+    "moe_b200_last_error",
+    "moe_b200_last_launch_count",
+)
+
+
+class MoeArgs(ctypes.Structure):
+    _fields_ = [
+        ("routing_logits", ctypes.c_void_p),
+        ("routing_bias", ctypes.c_void_p),
+        ("hidden_states", ctypes.c_void_p),
+        ("hidden_states_scale", ctypes.c_void_p),
+        ("gemm1_weights", ctypes.c_void_p),
+        ("gemm1_weights_scale", ctypes.c_void_p),
+        ("gemm2_weights", ctypes.c_void_p),
+        ("gemm2_weights_scale", ctypes.c_void_p),
+        ("output", ctypes.c_void_p),
+        ("num_tokens", ctypes.c_int32),
+        ("num_local_experts", ctypes.c_int32),
+        ("local_expert_offset", ctypes.c_int32),
+        ("routed_scaling_factor", ctypes.c_float),
+    ]
+
+
+class MoeLayout(ctypes.Structure):
+    _fields_ = [(name, ctypes.c_size_t) for name in (
+        "plan", "topk_idx", "topk_w", "tok_nloc", "tok_rows", "e_count", "e_start", "row_token",
+        "row_weight", "c_hi", "c_lo", "c_scale", "status", "r_max", "r_pad", "total")]
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded library (raises if it is missing)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise RuntimeError(
+            f"{LIB_PATH.name} is not built; run `python -m moe_swarm_b200.build` "
+            "(this package has no CPU or PyTorch fallback)")
+    l = ctypes.CDLL(str(LIB_PATH))
+    vp, sz, i32 = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int32
+    l.moe_b200_workspace_size.argtypes = [i32, i32]
+    l.moe_b200_workspace_size.restype = sz
+    l.moe_b200_workspace_layout.argtypes = [i32, i32, ctypes.POINTER(MoeLayout)]
+    l.moe_b200_workspace_layout.restype = ctypes.c_int
+    l.moe_b200_workspace_init.argtypes = [vp, sz, i32, i32, vp]
+    l.moe_b200_workspace_init.restype = ctypes.c_int
+    l.moe_b200_forward.argtypes = [ctypes.POINTER(MoeArgs), vp, sz, vp]
+    l.moe_b200_forward.restype = ctypes.c_int
+    l.moe_b200_route.argtypes = [ctypes.POINTER(MoeArgs), vp, sz, vp]
+    l.moe_b200_route.restype = ctypes.c_int
+    l.moe_b200_device_status.argtypes = [vp, sz, i32, i32, vp, i32]
+    l.moe_b200_device_status.restype = ctypes.c_int
+    l.moe_b200_last_error.argtypes = []
+    l.moe_b200_last_error.restype = ctypes.c_char_p
+    l.moe_b200_last_launch_count.argtypes = []
+    l.moe_b200_last_launch_count.restype = ctypes.c_int
+    _lib = l
+    return l
+
+
+def last_error() -> str:
+    return lib().moe_b200_last_error().decode(errors="replace")
+
+
+def layout(T: int, E: int) -> MoeLayout:
+    out = MoeLayout()
+    rc = lib().moe_b200_workspace_layout(int(T), int(E), ctypes.byref(out))
+    if rc != OK:
+        raise ValueError(f"moe_b200_workspace_layout({T}, {E}) failed: {last_error()}")
+    return out

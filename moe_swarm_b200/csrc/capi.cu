@@ -1,0 +1,306 @@
+// C ABI of the MoE layer: argument checks, workspace layout, TMA descriptors and the
+// launch sequence route -> [scatter] -> GEMM1 -> GEMM2 on the caller's stream.
+// No host synchronisation on the forward path; errors are status codes.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/moe_b200.h"
+#include "launch_args.cuh"
+#include "moe_internal.cuh"
+
+namespace moe {
+
+cudaError_t route_launch(const RouteArgs& a, cudaStream_t st, int* launches);
+cudaError_t gemm_prepare();
+cudaError_t gemm_launch(int mode, int grid, cudaStream_t st, const CUtensorMap& a, const CUtensorMap& a2,
+                        const CUtensorMap& b, const GemmArgs& g);
+
+}  // namespace moe
+
+namespace {
+
+thread_local std::string g_last_error;
+thread_local int g_last_launches = 0;
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(MOE_B200_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// Byte matrix [rows, cols] (row stride = cols bytes) read as 128x128-byte tiles, SWIZZLE_128B.
+bool encode_u8_2d(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols};
+  const cuuint32_t box[2] = {128, 128};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+struct DeviceInfo {
+  int sms = 0;
+  int major = 0;
+  bool smem_set = false;
+};
+
+DeviceInfo& device_info(int dev) {
+  static DeviceInfo info[64];
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lk(mu);
+  DeviceInfo& d = info[dev & 63];
+  if (d.sms == 0) {
+    cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev);
+  }
+  return d;
+}
+
+int check_args(const moe_b200_args* a) {
+  if (!a) return fail(MOE_B200_ERR_ARG, "null args");
+  if (a->num_tokens < 0) return fail(MOE_B200_ERR_ARG, "num_tokens < 0");
+  if (a->num_local_experts < 1 || a->num_local_experts > moe::kEG)
+    return fail(MOE_B200_ERR_ARG, "num_local_experts must be in [1, 256]");
+  if (a->num_tokens == 0) return MOE_B200_OK;
+  if (!a->routing_logits || !a->routing_bias || !a->hidden_states || !a->hidden_states_scale ||
+      !a->gemm1_weights || !a->gemm1_weights_scale || !a->gemm2_weights || !a->gemm2_weights_scale ||
+      !a->output)
+    return fail(MOE_B200_ERR_ARG, "null tensor pointer");
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (!al16(a->gemm1_weights) || !al16(a->gemm2_weights) || !al16(a->hidden_states) ||
+      !al16(a->routing_logits) || !al16(a->output))
+    return fail(MOE_B200_ERR_ARG, "weights, hidden states, logits and output must be 16-byte aligned");
+  return MOE_B200_OK;
+}
+
+moe::RouteArgs make_route_args(const moe_b200_args* a, uint8_t* ws, const moe::Layout& L, int sms) {
+  moe::RouteArgs r{};
+  r.logits = a->routing_logits;
+  r.bias = a->routing_bias;
+  r.hidden = a->hidden_states;
+  r.hs_scale = a->hidden_states_scale;
+  r.out = a->output;
+  r.T = a->num_tokens;
+  r.E = a->num_local_experts;
+  r.offset = a->local_expert_offset;
+  r.rsf = a->routed_scaling_factor;
+  r.nchunks = L.nchunks;
+  r.num_sms = sms;
+  r.r_split = static_cast<int>(L.r_max < (size_t)moe::kRSplit ? L.r_max : (size_t)moe::kRSplit);
+  r.r_pad = L.r_pad;
+  r.plan = reinterpret_cast<moe::Plan*>(ws + L.plan);
+  r.route_done = reinterpret_cast<int*>(ws + L.route_done);
+  r.topk_idx = reinterpret_cast<int*>(ws + L.topk_idx);
+  r.topk_w = reinterpret_cast<float*>(ws + L.topk_w);
+  r.tok_nloc = reinterpret_cast<int*>(ws + L.tok_nloc);
+  r.tok_le = reinterpret_cast<int*>(ws + L.tok_le);
+  r.tok_lw = reinterpret_cast<float*>(ws + L.tok_lw);
+  r.tok_rows = reinterpret_cast<int*>(ws + L.tok_rows);
+  r.chunk_hist = reinterpret_cast<int*>(ws + L.chunk_hist);
+  r.chunk_base = reinterpret_cast<int*>(ws + L.chunk_base);
+  r.e_count = reinterpret_cast<int*>(ws + L.e_count);
+  r.e_start = reinterpret_cast<int*>(ws + L.e_start);
+  r.e_mt_start = reinterpret_cast<int*>(ws + L.e_mt_start);
+  r.e_u1 = reinterpret_cast<int*>(ws + L.e_u1);
+  r.e_u2 = reinterpret_cast<int*>(ws + L.e_u2);
+  r.row_token = reinterpret_cast<int*>(ws + L.row_token);
+  r.row_weight = reinterpret_cast<float*>(ws + L.row_weight);
+  r.a_perm = ws + L.a_perm;
+  r.sa_perm = reinterpret_cast<float*>(ws + L.sa_perm);
+  return r;
+}
+
+int prepare(const moe_b200_args* a, void* workspace, size_t ws_bytes, moe::Layout* L, int* dev_out) {
+  int rc = check_args(a);
+  if (rc) return rc;
+  if (!moe::compute_layout(a->num_tokens, a->num_local_experts, L))
+    return fail(MOE_B200_ERR_ARG, "bad sizes");
+  if (!workspace || ws_bytes < L->total)
+    return fail(MOE_B200_ERR_WORKSPACE, "workspace too small: need " + std::to_string(L->total) + " bytes");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (device_info(dev).major != 10)
+    return fail(MOE_B200_ERR_DEVICE, "an sm_100 (B200-class) device is required");
+  *dev_out = dev;
+  return MOE_B200_OK;
+}
+
+int launch_route(const moe_b200_args* a, uint8_t* ws, const moe::Layout& L, int sms, cudaStream_t st,
+                 int* launches) {
+  moe::RouteArgs r = make_route_args(a, ws, L, sms);
+  cudaError_t e = moe::route_launch(r, st, launches);
+  if (e != cudaSuccess) return cuda_fail(e, "route launch");
+  return MOE_B200_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t moe_b200_workspace_size(int32_t num_tokens, int32_t num_local_experts) {
+  moe::Layout L;
+  if (!moe::compute_layout(num_tokens, num_local_experts, &L)) return 0;
+  return L.total;
+}
+
+int moe_b200_workspace_layout(int32_t num_tokens, int32_t num_local_experts, moe_b200_layout* out) {
+  moe::Layout L;
+  if (!out || !moe::compute_layout(num_tokens, num_local_experts, &L)) return fail(MOE_B200_ERR_ARG, "bad sizes");
+  out->plan = L.plan;
+  out->topk_idx = L.topk_idx;
+  out->topk_w = L.topk_w;
+  out->tok_nloc = L.tok_nloc;
+  out->tok_rows = L.tok_rows;
+  out->e_count = L.e_count;
+  out->e_start = L.e_start;
+  out->row_token = L.row_token;
+  out->row_weight = L.row_weight;
+  out->c_hi = L.c_hi;
+  out->c_lo = L.c_lo;
+  out->c_scale = L.c_scale;
+  out->status = L.status;
+  out->r_max = L.r_max;
+  out->r_pad = L.r_pad;
+  out->total = L.total;
+  return MOE_B200_OK;
+}
+
+int moe_b200_workspace_init(void* workspace, size_t ws_bytes, int32_t num_tokens, int32_t num_local_experts,
+                            void* stream) {
+  moe::Layout L;
+  if (!moe::compute_layout(num_tokens, num_local_experts, &L)) return fail(MOE_B200_ERR_ARG, "bad sizes");
+  if (!workspace || ws_bytes < L.total) return fail(MOE_B200_ERR_WORKSPACE, "workspace too small");
+  cudaError_t e = cudaMemsetAsync(static_cast<uint8_t*>(workspace) + L.counters_begin, 0,
+                                  L.counters_end - L.counters_begin, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync");
+  return MOE_B200_OK;
+}
+
+int moe_b200_route(const moe_b200_args* a, void* workspace, size_t ws_bytes, void* stream) {
+  moe::Layout L;
+  int dev = 0;
+  int rc = prepare(a, workspace, ws_bytes, &L, &dev);
+  if (rc) return rc;
+  if (a->num_tokens == 0) return MOE_B200_OK;
+  int launches = 0;
+  return launch_route(a, static_cast<uint8_t*>(workspace), L, device_info(dev).sms,
+                      static_cast<cudaStream_t>(stream), &launches);
+}
+
+int moe_b200_forward(const moe_b200_args* a, void* workspace, size_t ws_bytes, void* stream) {
+  g_last_launches = 0;
+  moe::Layout L;
+  int dev = 0;
+  int rc = prepare(a, workspace, ws_bytes, &L, &dev);
+  if (rc) return rc;
+  if (a->num_tokens == 0) return MOE_B200_OK;
+  DeviceInfo& di = device_info(dev);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  if (!di.smem_set) {
+    cudaError_t e1 = moe::gemm_prepare();
+    if (e1 != cudaSuccess) return cuda_fail(e1, "cudaFuncSetAttribute(gemm)");
+    di.smem_set = true;
+  }
+  int launches = 0;
+  rc = launch_route(a, ws, L, di.sms, st, &launches);
+  if (rc) return rc;
+
+  const int E = a->num_local_experts;
+  CUtensorMap mA1, mW13, mChi, mClo, mW2;
+  if (!encode_u8_2d(&mA1, ws + L.a_perm, moe::kH, L.r_pad) ||
+      !encode_u8_2d(&mW13, a->gemm1_weights, moe::kH, (uint64_t)E * moe::kN1) ||
+      !encode_u8_2d(&mChi, ws + L.c_hi, moe::kI, L.r_pad) || !encode_u8_2d(&mClo, ws + L.c_lo, moe::kI, L.r_pad) ||
+      !encode_u8_2d(&mW2, a->gemm2_weights, moe::kI, (uint64_t)E * moe::kH))
+    return fail(MOE_B200_ERR_CUDA, "cuTensorMapEncodeTiled failed");
+
+  moe::GemmArgs g{};
+  g.plan = reinterpret_cast<const moe::Plan*>(ws + L.plan);
+  g.e_count = reinterpret_cast<const int*>(ws + L.e_count);
+  g.e_start = reinterpret_cast<const int*>(ws + L.e_start);
+  g.e_mt_start = reinterpret_cast<const int*>(ws + L.e_mt_start);
+  g.E = E;
+  g.r_split = static_cast<int>(L.r_max < (size_t)moe::kRSplit ? L.r_max : (size_t)moe::kRSplit);
+  g.r_pad = L.r_pad;
+  g.c_hi = ws + L.c_hi;
+  g.c_lo = ws + L.c_lo;
+  g.c_scale = reinterpret_cast<float*>(ws + L.c_scale);
+  g.part1 = reinterpret_cast<float*>(ws + L.part1);
+  g.cnt1 = reinterpret_cast<int*>(ws + L.cnt1);
+  g.row_token = reinterpret_cast<const int*>(ws + L.row_token);
+  g.row_weight = reinterpret_cast<const float*>(ws + L.row_weight);
+  g.tok_nloc = reinterpret_cast<const int*>(ws + L.tok_nloc);
+  g.tok_rows = reinterpret_cast<const int*>(ws + L.tok_rows);
+  g.part2 = reinterpret_cast<float*>(ws + L.part2);
+  g.cnt2 = reinterpret_cast<int*>(ws + L.cnt2);
+  g.out = a->output;
+  g.status = reinterpret_cast<int*>(ws + L.status);
+
+  moe::GemmArgs g1 = g;
+  g1.e_ustart = reinterpret_cast<const int*>(ws + L.e_u1);
+  g1.sa = reinterpret_cast<const float*>(ws + L.sa_perm);
+  g1.sw = a->gemm1_weights_scale;
+  cudaError_t e = moe::gemm_launch(1, di.sms, st, mA1, mA1, mW13, g1);
+  if (e != cudaSuccess) return cuda_fail(e, "gemm1 launch");
+  ++launches;
+  moe::GemmArgs g2 = g;
+  g2.e_ustart = reinterpret_cast<const int*>(ws + L.e_u2);
+  g2.sa = reinterpret_cast<const float*>(ws + L.c_scale);
+  g2.sw = a->gemm2_weights_scale;
+  e = moe::gemm_launch(2, di.sms, st, mChi, mClo, mW2, g2);
+  if (e != cudaSuccess) return cuda_fail(e, "gemm2 launch");
+  ++launches;
+  g_last_launches = launches;
+  return MOE_B200_OK;
+}
+
+int moe_b200_device_status(void* workspace, size_t ws_bytes, int32_t num_tokens, int32_t num_local_experts,
+                           void* stream, int32_t clear) {
+  moe::Layout L;
+  if (!moe::compute_layout(num_tokens, num_local_experts, &L)) return -fail(MOE_B200_ERR_ARG, "bad sizes");
+  if (!workspace || ws_bytes < L.total) return -fail(MOE_B200_ERR_WORKSPACE, "workspace too small");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int v = 0;
+  int* p = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + L.status);
+  cudaError_t e = cudaMemcpyAsync(&v, p, sizeof(int), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e == cudaSuccess && clear) e = cudaMemsetAsync(p, 0, sizeof(int), st);
+  if (e != cudaSuccess) return -cuda_fail(e, "device status");
+  return v;
+}
+
+const char* moe_b200_last_error(void) { return g_last_error.c_str(); }
+
+int moe_b200_last_launch_count(void) { return g_last_launches; }
+
+}  // extern "C"

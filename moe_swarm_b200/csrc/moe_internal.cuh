@@ -1,0 +1,118 @@
+// Shared constants, the device-side plan and the workspace layout of one layer call.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+
+namespace moe {
+
+constexpr int kH = 7168;          // hidden size
+constexpr int kI = 2048;          // intermediate size
+constexpr int kN1 = 2 * kI;       // GEMM1 output rows per expert (X1 | X2)
+constexpr int kEG = 256;          // global experts
+constexpr int kTopK = 8;
+constexpr int kNGroup = 8;
+constexpr int kTopKGroup = 4;
+constexpr int kBlk = 128;         // quantisation block edge
+constexpr int kKB1 = kH / kBlk;   // 56 K-blocks of GEMM1
+constexpr int kKB2 = kI / kBlk;   // 16 K-blocks of GEMM2
+constexpr int kNT1 = kI / kBlk;   // 16 GEMM1 tiles (128 X1 + 128 X2 rows each)
+constexpr int kNT2 = kH / kBlk;   // 56 GEMM2 tiles (128 output features each)
+
+constexpr int kChunk = 128;       // tokens per routing CTA
+constexpr int kRouteThreads = 512;
+constexpr int kRSplit = 256;      // split-K is considered only when rows <= kRSplit
+constexpr int kS1Max = 14;        // GEMM1 split factors: divisors of 56 up to 14
+constexpr int kS2Max = 8;         // GEMM2 split factors: divisors of 16 up to 8
+
+// Device status codes (first one wins).
+enum : int {
+  kStOk = 0,
+  kStWaitProducer = 0x101,
+  kStWaitMma = 0x102,
+  kStWaitMmaTmem = 0x103,
+  kStWaitEpilogue = 0x104,
+  kStWaitDrain = 0x105,
+};
+
+// Written by the routing scan, read by the GEMM kernels.
+struct Plan {
+  int T, E, rows, m_tiles;
+  int s1, kb1, units1;    // GEMM1 split factor, K-blocks per split, work units
+  int s2, kb2, units2;    // GEMM2
+  int pad[6];
+};
+
+struct Layout {
+  int T, E, nchunks;
+  size_t r_max, r_pad, mt_max;
+  // offsets in bytes
+  size_t plan, route_done, status;
+  size_t topk_idx, topk_w, tok_nloc, tok_le, tok_lw, tok_rows;
+  size_t chunk_hist, chunk_base;
+  size_t e_count, e_start, e_mt_start, e_u1, e_u2;
+  size_t row_token, row_weight;
+  size_t a_perm, sa_perm;
+  size_t c_hi, c_lo, c_scale;
+  size_t part1, cnt1, part2, cnt2;
+  size_t counters_begin, counters_end;   // region zeroed by workspace_init
+  size_t total;
+};
+
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+inline bool compute_layout(int T, int E, Layout* L) {
+  if (T < 0 || E < 1 || E > kEG) return false;
+  Layout l{};
+  l.T = T;
+  l.E = E;
+  l.nchunks = (T + kChunk - 1) / kChunk;
+  const size_t tt = T > 0 ? T : 1;
+  const size_t per_tok = E < kTopK ? E : kTopK;
+  l.r_max = tt * per_tok;
+  l.r_pad = align_up(l.r_max, 32);
+  l.mt_max = (l.r_max + kBlk - 1) / kBlk + E;
+  const size_t r_split = l.r_max < (size_t)kRSplit ? l.r_max : (size_t)kRSplit;
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    size_t at = align_up(o, 1024);
+    o = at + bytes;
+    return at;
+  };
+  l.plan = take(sizeof(Plan));
+  // self-resetting counters and the status word live together so one memset clears them
+  l.counters_begin = align_up(o, 1024);
+  l.route_done = take(sizeof(int));
+  l.status = take(sizeof(int));
+  l.cnt1 = take(l.mt_max * kNT1 * sizeof(int));
+  l.cnt2 = take(tt * kNT2 * 2 * sizeof(int));
+  l.counters_end = align_up(o, 1024);
+  l.topk_idx = take(tt * kTopK * sizeof(int));
+  l.topk_w = take(tt * kTopK * sizeof(float));
+  l.tok_nloc = take(tt * sizeof(int));
+  l.tok_le = take(tt * kTopK * sizeof(int));
+  l.tok_lw = take(tt * kTopK * sizeof(float));
+  l.tok_rows = take(tt * kTopK * sizeof(int));
+  l.chunk_hist = take((size_t)(l.nchunks > 0 ? l.nchunks : 1) * E * sizeof(int));
+  l.chunk_base = take((size_t)(l.nchunks > 0 ? l.nchunks : 1) * E * sizeof(int));
+  l.e_count = take((size_t)E * sizeof(int));
+  l.e_start = take((size_t)(E + 1) * sizeof(int));
+  l.e_mt_start = take((size_t)(E + 1) * sizeof(int));
+  l.e_u1 = take((size_t)(E + 1) * sizeof(int));
+  l.e_u2 = take((size_t)(E + 1) * sizeof(int));
+  l.row_token = take(l.r_pad * sizeof(int));
+  l.row_weight = take(l.r_pad * sizeof(float));
+  l.a_perm = take(l.r_pad * kH);
+  l.sa_perm = take((size_t)kKB1 * l.r_pad * sizeof(float));
+  l.c_hi = take(l.r_pad * kI);
+  l.c_lo = take(l.r_pad * kI);
+  l.c_scale = take((size_t)kKB2 * l.r_pad * sizeof(float));
+  l.part1 = take((size_t)kS1Max * r_split * kN1 * sizeof(float));
+  const size_t p2_rows = l.r_pad > (size_t)kS2Max * r_split ? l.r_pad : (size_t)kS2Max * r_split;
+  l.part2 = take(p2_rows * kH * sizeof(float));
+  l.total = align_up(o, 1024);
+  *L = l;
+  return true;
+}
+
+}  // namespace moe

@@ -1,0 +1,376 @@
+// DeepSeek-V3 no-aux routing fused with the token->expert histogram, the
+// prefix sum and the permutation of activation rows into expert-major order.
+//
+// Semantics follow spec/reference_official.py:95-126 (selection on
+// sigmoid(logits)+bias, 8 groups scored by their top-2 sum, 4 groups kept,
+// top-8 experts, bias-free weights normalised then scaled) and the row order
+// of reference/kernel_pytorch_v1.py:100-123 (stable sort by local expert:
+// expert-major, token-minor).  The reference's Triton kernel appends picks to
+// per-expert buckets with atomics (solution/python/kernel.py:137-213), which
+// makes the row order run-dependent; here every row index is a prefix count,
+// so the permutation is deterministic and identical to the oracle's.
+//
+// Work split: one warp per token; lane l owns experts 8l..8l+7, so the four
+// lanes 4g..4g+3 own group g.  A CTA routes a chunk of 128 tokens and keeps
+// per-expert token bitmasks of its chunk in shared memory; the rank of a token
+// inside an expert's segment is a popcount over those masks plus the chunk's
+// base.  With one chunk (T <= 128, the decode regime) a single CTA does
+// routing, scan and scatter in one launch; otherwise the last CTA to finish
+// routing performs the scan and a second kernel scatters.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "launch_args.cuh"
+#include "moe_internal.cuh"
+#include "ptx.cuh"
+
+namespace moe {
+
+
+__device__ __forceinline__ uint32_t orderable(float v) {
+  uint32_t u = __float_as_uint(v);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__device__ __forceinline__ float bf16_bits_to_float(uint16_t b) {
+  return __uint_as_float(static_cast<uint32_t>(b) << 16);
+}
+
+__device__ __forceinline__ int warp_excl_prefix(int v, int lane) {
+  int x = v;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    int y = __shfl_up_sync(0xffffffffu, x, d);
+    if (lane >= d) x += y;
+  }
+  return x - v;
+}
+
+// Routes token t with the calling warp; records it in the chunk's histogram and masks.
+__device__ void route_token(const RouteArgs& a, const float* s_bias, int t, int tl, int lane,
+                            int* s_hist, uint32_t (*s_mask)[kChunk / 32]) {
+  const float* lg = a.logits + static_cast<size_t>(t) * kEG + lane * 8;
+  const float4 v0 = *reinterpret_cast<const float4*>(lg);
+  const float4 v1 = *reinterpret_cast<const float4*>(lg + 4);
+  const float x[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+  float s[8], sb[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    // sigmoid as 1/(1+exp(-x)) in fp32 (reference_official.py:99); exp is evaluated in
+    // double and rounded once so it is the correctly rounded fp32 exponential.
+    const float e = static_cast<float>(exp(-static_cast<double>(x[i])));
+    s[i] = 1.0f / (1.0f + e);
+    sb[i] = s[i] + s_bias[lane * 8 + i];
+  }
+  // group score: sum of the group's top-2 selection scores (multiset top-2)
+  float m1 = -INFINITY, m2 = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float v = sb[i];
+    if (v > m1) { m2 = m1; m1 = v; } else if (v > m2) { m2 = v; }
+  }
+#pragma unroll
+  for (int d = 1; d <= 2; d <<= 1) {
+    const float o1 = __shfl_xor_sync(0xffffffffu, m1, d);
+    const float o2 = __shfl_xor_sync(0xffffffffu, m2, d);
+    const float n1 = fmaxf(m1, o1);
+    const float n2 = fmaxf(fminf(m1, o1), fmaxf(m2, o2));
+    m1 = n1;
+    m2 = n2;
+  }
+  const float gscore = m1 + m2;
+  const int g = lane >> 2;
+  int rank = 0;
+#pragma unroll
+  for (int h = 0; h < kNGroup; ++h) {
+    const float o = __shfl_sync(0xffffffffu, gscore, h * 4);
+    rank += (o > gscore || (o == gscore && h < g)) ? 1 : 0;
+  }
+  const bool keep = rank < kTopKGroup;
+  // top-8 among kept groups: 8 rounds of a warp-wide argmax (ties -> lower expert id)
+  uint32_t taken = 0;
+#pragma unroll 1
+  for (int r = 0; r < kTopK; ++r) {
+    uint64_t best = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float v = keep ? sb[i] : -3.402823466e38f;
+      const uint64_t key = (static_cast<uint64_t>(orderable(v)) << 32) |
+                           static_cast<uint64_t>(0xFFFFu - (lane * 8 + i));
+      const bool free_slot = ((taken >> i) & 1u) == 0;
+      if (free_slot && key > best) best = key;
+    }
+#pragma unroll
+    for (int d = 16; d >= 1; d >>= 1) {
+      const uint64_t o = __shfl_xor_sync(0xffffffffu, best, d);
+      best = o > best ? o : best;
+    }
+    const int id = 0xFFFF - static_cast<int>(best & 0xFFFFu);
+    if ((id >> 3) == lane) taken |= 1u << (id & 7);
+  }
+  // combine weights from s (no bias): s / (sum + 1e-20) * rsf (reference_official.py:122-126)
+  float part = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    if ((taken >> i) & 1u) part += s[i];
+#pragma unroll
+  for (int d = 16; d >= 1; d >>= 1) part += __shfl_xor_sync(0xffffffffu, part, d);
+  const float denom = part + 1e-20f;
+
+  const int lo_g = a.offset, hi_g = a.offset + a.E;
+  uint32_t local_mask = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int ge = lane * 8 + i;
+    if (((taken >> i) & 1u) && ge >= lo_g && ge < hi_g) local_mask |= 1u << i;
+  }
+  int pos = warp_excl_prefix(__popc(taken), lane);
+  int lpos = warp_excl_prefix(__popc(local_mask), lane);
+  int* idx_out = a.topk_idx + static_cast<size_t>(t) * kTopK;
+  float* w_out = a.topk_w + static_cast<size_t>(t) * kTopK;
+  int* le_out = a.tok_le + static_cast<size_t>(t) * kTopK;
+  float* lw_out = a.tok_lw + static_cast<size_t>(t) * kTopK;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    if ((taken >> i) & 1u) {
+      const int ge = lane * 8 + i;
+      const float w = (s[i] / denom) * a.rsf;
+      idx_out[pos] = ge;
+      w_out[pos] = w;
+      ++pos;
+      if ((local_mask >> i) & 1u) {
+        const int le = ge - lo_g;
+        le_out[lpos] = le;
+        lw_out[lpos] = w;
+        ++lpos;
+        atomicAdd(&s_hist[le], 1);
+        atomicOr(&s_mask[le][tl >> 5], 1u << (tl & 31));
+      }
+    }
+  }
+  int nloc = __popc(local_mask);
+#pragma unroll
+  for (int d = 16; d >= 1; d >>= 1) nloc += __shfl_xor_sync(0xffffffffu, nloc, d);
+  if (lane == 0) a.tok_nloc[t] = nloc;
+}
+
+// Scatters the local picks of token t (chunk c, index tl in the chunk) with the calling warp:
+// row indices, row metadata, the fp8 activation row and its 56 scales.  A token with no
+// local expert gets a zero output row instead.
+__device__ void scatter_token(const RouteArgs& a, int t, int tl, int c, int lane,
+                              const uint32_t (*s_mask)[kChunk / 32], const int* base) {
+  const int k = a.tok_nloc[t];
+  if (k == 0) {
+    uint4* dst = reinterpret_cast<uint4*>(a.out + static_cast<size_t>(t) * kH);
+    for (int j = lane; j < kH * 2 / 16; j += 32) dst[j] = make_uint4(0, 0, 0, 0);
+    return;
+  }
+  int row = 0;
+  if (lane < k) {
+    const int le = a.tok_le[static_cast<size_t>(t) * kTopK + lane];
+    const float w = a.tok_lw[static_cast<size_t>(t) * kTopK + lane];
+    int rank = 0;
+    for (int wd = 0; wd < (tl >> 5); ++wd) rank += __popc(s_mask[le][wd]);
+    rank += __popc(s_mask[le][tl >> 5] & ((1u << (tl & 31)) - 1u));
+    row = base[le] + rank;
+    a.row_token[row] = t;
+    a.row_weight[row] = w;
+    a.tok_rows[static_cast<size_t>(t) * kTopK + lane] = row;
+  }
+  int rows[kTopK];
+#pragma unroll
+  for (int i = 0; i < kTopK; ++i) rows[i] = __shfl_sync(0xffffffffu, row, i);
+  const uint4* src = reinterpret_cast<const uint4*>(a.hidden + static_cast<size_t>(t) * kH);
+  for (int j = lane; j < kH / 16; j += 32) {
+    const uint4 v = __ldg(src + j);
+#pragma unroll
+    for (int i = 0; i < kTopK; ++i)
+      if (i < k) reinterpret_cast<uint4*>(a.a_perm + static_cast<size_t>(rows[i]) * kH)[j] = v;
+  }
+  for (int kb = lane; kb < kKB1; kb += 32) {
+    const float sc = a.hs_scale[static_cast<size_t>(kb) * a.T + t];
+#pragma unroll
+    for (int i = 0; i < kTopK; ++i)
+      if (i < k) a.sa_perm[static_cast<size_t>(kb) * a.r_pad + rows[i]] = sc;
+  }
+}
+
+__device__ __forceinline__ float split_efficiency(int units, int sms) {
+  const int waves = (units + sms - 1) / sms;
+  return static_cast<float>(units) / static_cast<float>(waves * sms);
+}
+
+// Picks the split factor with the best last-wave fill; smaller splits win near-ties.
+__device__ int choose_split(int base_units, int sms, const int* cands, int ncand) {
+  int best = cands[0];
+  float best_eff = split_efficiency(base_units * cands[0], sms);
+  for (int i = 1; i < ncand; ++i) {
+    const float e = split_efficiency(base_units * cands[i], sms);
+    if (e > best_eff + 0.03f) {
+      best_eff = e;
+      best = cands[i];
+    }
+  }
+  return best;
+}
+
+// Expert counts -> segment starts, per-chunk bases, m-tile prefix, split factors, plan.
+// Executed by one whole CTA.  `hist(c, e)` reads the chunk histogram.
+template <typename Hist>
+__device__ void scan_plan(const RouteArgs& a, Hist hist, int* s_tmp, int* s_start) {
+  const int tid = threadIdx.x;
+  const int E = a.E;
+  int cnt = 0;
+  if (tid < E)
+    for (int c = 0; c < a.nchunks; ++c) cnt += hist(c, tid);
+  // exclusive scans over experts of rows and of m-tiles (E <= 256 < blockDim)
+  int* s_cnt = s_tmp;
+  int* s_mt = s_tmp + 256;
+  if (tid < 256) {
+    s_cnt[tid] = tid < E ? cnt : 0;
+    s_mt[tid] = tid < E ? (cnt + kBlk - 1) / kBlk : 0;
+  }
+  __syncthreads();
+  for (int d = 1; d < 256; d <<= 1) {
+    int vc = 0, vm = 0;
+    if (tid < 256 && tid >= d) {
+      vc = s_cnt[tid - d];
+      vm = s_mt[tid - d];
+    }
+    __syncthreads();
+    if (tid < 256 && tid >= d) {
+      s_cnt[tid] += vc;
+      s_mt[tid] += vm;
+    }
+    __syncthreads();
+  }
+  // s_cnt / s_mt now hold inclusive prefixes
+  const int rows = s_cnt[255];
+  const int mtiles = s_mt[255];
+  __shared__ int s_split[2];
+  if (tid == 0) {
+    int s1 = 1, s2 = 1;
+    if (rows <= kRSplit && rows > 0) {
+      const int c1[] = {1, 2, 4, 7, 8, 14};
+      const int c2[] = {1, 2, 4, 8};
+      s1 = choose_split(mtiles * kNT1, a.num_sms, c1, 6);
+      s2 = choose_split(mtiles * kNT2, a.num_sms, c2, 4);
+    }
+    s_split[0] = s1;
+    s_split[1] = s2;
+    Plan p{};
+    p.T = a.T;
+    p.E = E;
+    p.rows = rows;
+    p.m_tiles = mtiles;
+    p.s1 = s1;
+    p.kb1 = kKB1 / s1;
+    p.units1 = mtiles * kNT1 * s1;
+    p.s2 = s2;
+    p.kb2 = kKB2 / s2;
+    p.units2 = mtiles * kNT2 * s2;
+    *a.plan = p;
+  }
+  __syncthreads();
+  const int s1 = s_split[0], s2 = s_split[1];
+  if (tid < E) {
+    const int start = s_cnt[tid] - cnt;
+    const int mt0 = s_mt[tid] - (cnt + kBlk - 1) / kBlk;
+    s_start[tid] = start;
+    a.e_count[tid] = cnt;
+    a.e_start[tid] = start;
+    a.e_mt_start[tid] = mt0;
+    a.e_u1[tid] = mt0 * kNT1 * s1;
+    a.e_u2[tid] = mt0 * kNT2 * s2;
+    int run = start;
+    for (int c = 0; c < a.nchunks; ++c) {
+      a.chunk_base[static_cast<size_t>(c) * E + tid] = run;
+      run += hist(c, tid);
+    }
+  }
+  if (tid == 0) {
+    a.e_start[E] = rows;
+    a.e_mt_start[E] = mtiles;
+    a.e_u1[E] = mtiles * kNT1 * s1;
+    a.e_u2[E] = mtiles * kNT2 * s2;
+  }
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(kRouteThreads, 1) route_kernel(RouteArgs a) {
+  __shared__ float s_bias[kEG];
+  __shared__ int s_hist[kEG];
+  __shared__ uint32_t s_mask[kEG][kChunk / 32];
+  __shared__ int s_tmp[512];
+  __shared__ int s_start[kEG];
+  __shared__ int s_last;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int c = blockIdx.x;
+  for (int i = tid; i < kEG; i += blockDim.x) {
+    s_bias[i] = bf16_bits_to_float(a.bias[i]);
+    s_hist[i] = 0;
+  }
+  for (int i = tid; i < kEG * (kChunk / 32); i += blockDim.x) (&s_mask[0][0])[i] = 0;
+  __syncthreads();
+  const int t0 = c * kChunk;
+  const int nt = min(kChunk, a.T - t0);
+  for (int tl = warp; tl < nt; tl += kRouteThreads / 32)
+    route_token(a, s_bias, t0 + tl, tl, lane, s_hist, s_mask);
+  __syncthreads();
+  if (a.nchunks == 1) {
+    scan_plan(a, [&](int, int e) { return s_hist[e]; }, s_tmp, s_start);
+    for (int tl = warp; tl < nt; tl += kRouteThreads / 32)
+      scatter_token(a, t0 + tl, tl, 0, lane, s_mask, s_start);
+    return;
+  }
+  for (int e = tid; e < a.E; e += blockDim.x) a.chunk_hist[static_cast<size_t>(c) * a.E + e] = s_hist[e];
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const int prev = atomicAdd(a.route_done, 1);
+    s_last = (prev == a.nchunks - 1);
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const int* hist = a.chunk_hist;
+  const int E = a.E;
+  scan_plan(a, [&](int cc, int e) { return __ldcg(hist + static_cast<size_t>(cc) * E + e); }, s_tmp,
+            s_start);
+  if (tid == 0) *a.route_done = 0;   // self-reset for the next call
+}
+
+__global__ void __launch_bounds__(kRouteThreads, 1) scatter_kernel(RouteArgs a) {
+  __shared__ uint32_t s_mask[kEG][kChunk / 32];
+  __shared__ int s_base[kEG];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int c = blockIdx.x;
+  for (int i = tid; i < kEG * (kChunk / 32); i += blockDim.x) (&s_mask[0][0])[i] = 0;
+  for (int e = tid; e < a.E; e += blockDim.x) s_base[e] = a.chunk_base[static_cast<size_t>(c) * a.E + e];
+  __syncthreads();
+  const int t0 = c * kChunk;
+  const int nt = min(kChunk, a.T - t0);
+  for (int tl = warp; tl < nt; tl += kRouteThreads / 32) {
+    const int t = t0 + tl;
+    const int k = a.tok_nloc[t];
+    if (lane < k) {
+      const int le = a.tok_le[static_cast<size_t>(t) * kTopK + lane];
+      atomicOr(&s_mask[le][tl >> 5], 1u << (tl & 31));
+    }
+  }
+  __syncthreads();
+  for (int tl = warp; tl < nt; tl += kRouteThreads / 32)
+    scatter_token(a, t0 + tl, tl, c, lane, s_mask, s_base);
+}
+
+cudaError_t route_launch(const RouteArgs& a, cudaStream_t st, int* launches) {
+  route_kernel<<<a.nchunks, kRouteThreads, 0, st>>>(a);
+  ++*launches;
+  if (a.nchunks > 1) {
+    scatter_kernel<<<a.nchunks, kRouteThreads, 0, st>>>(a);
+    ++*launches;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace moe

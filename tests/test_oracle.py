@@ -1,0 +1,116 @@
+"""CPU: the oracle is pinned to outputs of the reference itself (tests/golden).
+
+Follows the reference's own CPU tests (test_kernel.py:57-143): routing against the
+routing lifted from the official reference, the (token, local expert) pair set of the
+compaction, block dequantisation and the SwiGLU half order -- plus whole-layer outputs
+of spec/reference_official.run and reference/kernel_pytorch_v1.kernel.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from moe_swarm_b200 import workload as W
+from oracle import moe_ref as O
+from tests import _cases as C
+
+torch.set_num_threads(max(1, torch.get_num_threads()))
+
+
+@pytest.mark.parametrize("path", C.route_fixtures(), ids=lambda p: p.stem)
+def test_route_matches_reference_golden(path):
+    z = np.load(path)
+    x = W.make_activations(int(z["T"]), int(z["seed"]), skew=float(z["skew"]))
+    assert C.activation_digest(x) == str(z["act_sha"])
+    idx, w = O.route(x["routing_logits"], x["routing_bias"], float(z["rsf"]))
+    ids = idx.sort(dim=1).values
+    assert torch.equal(ids, torch.from_numpy(z["topk_sorted"].astype(np.int64)))
+    ws = torch.gather(w, 1, ids)
+    torch.testing.assert_close(ws, torch.from_numpy(z["w_sorted"]), rtol=0, atol=0)
+    # v1's routing (torch.sigmoid) selects the same experts (reference test_kernel.py:67-69)
+    assert torch.equal(ids, torch.from_numpy(z["topk_sorted_v1"].astype(np.int64)))
+    # 8 picks per token whose weights sum to rsf (test_kernel.py:73-74)
+    assert torch.equal((w > 0).sum(1), torch.full((w.shape[0],), 8))
+    torch.testing.assert_close(w.sum(1), torch.full((w.shape[0],), float(z["rsf"])), rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("path", C.layer_fixtures(), ids=lambda p: p.stem)
+def test_layer_matches_reference_golden(path):
+    x, g = C.load_layer_case(path)
+    out = O.run(**x)
+    assert torch.equal(out.view(torch.int16), g["official"].view(torch.int16)), \
+        "oracle differs from spec/reference_official.run"
+    out_v1 = O.run_v1(**x)
+    assert torch.equal(out_v1.view(torch.int16), g["v1"].view(torch.int16)), \
+        "oracle v1 restatement differs from reference/kernel_pytorch_v1.kernel"
+
+
+@pytest.mark.parametrize("T,offset", [(1, 0), (7, 32), (56, 224), (129, 96)])
+def test_local_permutation_pair_set(T, offset):
+    """Every (token, local expert) pair exactly once with its weight (test_kernel.py:78-112),
+    in expert-major, token-minor order."""
+    torch.manual_seed(1)
+    logits = torch.randn(T, 256)
+    bias = torch.randn(256).to(torch.bfloat16)
+    idx, w = O.route(logits, bias, 1.0)
+    tok, le, ww, counts = O.local_permutation(idx, w, offset, 32)
+    assert int(counts.sum()) == tok.numel()
+    expected = {(t, int(e) - offset) for t in range(T) for e in idx[t].tolist()
+                if offset <= int(e) < offset + 32}
+    got = set(zip(tok.tolist(), le.tolist()))
+    assert got == expected and len(got) == tok.numel()
+    key = le * T + tok
+    assert torch.all(key[1:] > key[:-1])
+    for t, e, wt in zip(tok.tolist(), le.tolist(), ww.tolist()):
+        assert wt == float(w[t, offset + e])
+
+
+def test_dequant_block_scale():
+    torch.manual_seed(2)
+    w = torch.randn(256, 384)
+    s = torch.rand(2, 3) + 0.5
+    naive = w * torch.repeat_interleave(torch.repeat_interleave(s, 128, 0), 128, 1)
+    torch.testing.assert_close(O.dequant_blocks(w, s), naive, rtol=0, atol=0)
+
+
+def test_swiglu_half_order():
+    """silu goes on the SECOND half, multiplied by the first (test_kernel.py:130-143)."""
+    torch.manual_seed(3)
+    A = torch.randn(4, 8)
+    W13 = torch.eye(2 * 2048, 8)[:, :8] * 0 + torch.randn(2 * 2048, 8)
+    W2 = torch.randn(8, 2048)
+    G1 = A @ W13.t()
+    x1, x2 = G1[:, :2048], G1[:, 2048:]
+    want = (x2 / (1 + torch.exp(-x2)) * x1) @ W2.t()
+    torch.testing.assert_close(O.expert_forward(A, W13, W2), want, rtol=1e-5, atol=1e-5)
+    swapped = (x1 / (1 + torch.exp(-x1)) * x2) @ W2.t()
+    assert not torch.allclose(want, swapped)
+
+
+def test_generator_is_deterministic_and_lazy():
+    a = W.make_expert(7, 40)
+    b = W.make_weights(32, 32, 7, experts=[8])
+    assert torch.equal(a[0].view(torch.uint8), b["gemm1_weights"][8].view(torch.uint8))
+    assert torch.equal(a[3], b["gemm2_weights_scale"][8])
+    x1 = W.make_activations(5, 3)
+    x2 = W.make_activations(5, 3)
+    for k in x1:
+        assert torch.equal(x1[k].view(torch.uint8) if x1[k].dtype != torch.float32 else x1[k],
+                           x2[k].view(torch.uint8) if x2[k].dtype != torch.float32 else x2[k])
+
+
+def test_quantisation_layouts():
+    x = torch.randn(3, 7168)
+    q, s = W.quantize_tokens(x)
+    assert q.dtype == torch.float8_e4m3fn and s.shape == (56, 3)
+    deq = q.float().view(3, 56, 128) * s.t().unsqueeze(2)
+    assert torch.allclose(deq.view(3, 7168), x, rtol=0.07, atol=1e-3)
+    assert float(q.float().abs().max()) == 448.0
+
+
+def test_parity_report_counts_planted_miss():
+    ref = torch.zeros(4, 4)
+    got = ref.clone()
+    got[1, 2] = 0.5                      # a planted error on the CPU side
+    r = O.parity_report(got, ref)
+    assert r["bad"] == 1 and r["max_abs"] == 0.5
