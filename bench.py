@@ -1,0 +1,467 @@
+"""Benchmark of the B200 DeepSeek-V3 FP8 block-scale MoE layer.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...   (expert parallelism, one rank per GPU)
+
+Workload (every N): the expert-parallel full layer of the benchmark configs -- T=4096
+tokens, all 256 DeepSeek-V3 experts sharded 256/N per GPU through local_expert_offset,
+hidden states / logits replicated on every rank, the bf16 partial outputs combined by an
+NCCL reduce-scatter (rows T/N per rank).  At N=1 one GPU holds all 256 experts.  The
+total work is fixed as N grows ("scaling": "strong").  A step is one layer call plus the
+reduce-scatter; `value` is whole-job tokens/s = T / step time (max over ranks).
+
+At N=1 the line also carries the single-GPU sweeps with 32 local experts: decode
+T in {1,7,16,32,64,80} (HBM-bound), mid-batch T=901 with skewed routing, and prefill
+T in {8192,16384} (tensor-bound), each timed per call after an L2 flush.
+
+Inputs are synthetic (seeded, distributions of the benchmark configs); weights are
+random-init on the device.  `--impl reference` times the CPU oracle port of the
+reference's PyTorch kernel (reference/kernel_pytorch_v1.py) on the host cores.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = ("MoE-layer latency (µs) & tokens/s vs T; HBM/FP8-tensor roofline fraction; "
+          "EP 1/2/4/8")
+H, I, E_GLOBAL = 7168, 2048, 256
+W13_BYTES = 2 * I * H          # fp8 bytes of one expert's gate/up weights
+W2_BYTES = H * I
+S13_BYTES = 32 * 56 * 4
+S2_BYTES = 56 * 16 * 4
+FLOP_PER_ASSIGN = 2 * (H * 2 * I) + 2 * (I * H)   # 88,080,384 (GEMM1 + GEMM2)
+EP_T = 4096
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clock/throttle samples during the timed region (read-only queries)."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self):
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                                         text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, ValueError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self, gpus):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                idx = int(f[0])
+                if gpus is not None and idx not in gpus:
+                    continue
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() in ("active", "1"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        sm.sort()
+        loaded = [s for s in sm if s > 0.5 * mx] or sm
+        return {"sm_mhz": loaded[len(loaded) // 2], "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- workload
+def ep_inputs(rank, world, device, seed=0):
+    import moe_swarm_b200.workload as W
+    E_local = E_GLOBAL // world
+    act = W.make_activations(EP_T, seed)
+    x = {k: v.to(device) for k, v in act.items()}
+    x.update(W.make_weights_fast(E_local, seed * 1000 + rank, device=device))
+    x["local_expert_offset"] = rank * E_local
+    x["routed_scaling_factor"] = 2.5
+    return x, act
+
+
+def routing_facts(x):
+    """Exact active experts / rows of this rank from the device routing (outside timing)."""
+    import moe_swarm_b200 as M
+    r = M.route(**x)
+    counts = r["e_count"].cpu()
+    T = x["routing_logits"].shape[0]
+    return {"active": int((counts > 0).sum()), "rows": int(counts.sum()), "T": T,
+            "e_count": counts}
+
+
+def gemm_bytes(f):
+    """Algorithmic HBM bytes per launch of each GEMM (each weight byte and each activation
+    byte once; outputs once)."""
+    a, R, T = f["active"], f["rows"], f["T"]
+    g1 = a * (W13_BYTES + S13_BYTES) + R * (H + 56 * 4) + R * (2 * I + 16 * 4)
+    g2 = a * (W2_BYTES + S2_BYTES) + R * (2 * I + 16 * 4) + T * H * 2
+    return g1, g2
+
+
+# ----------------------------------------------------------------------------- timers
+class StageTimer:
+    def __init__(self):
+        from moe_swarm_b200 import _native as N
+        self.N = N
+        self.lib = N.lib()
+        self.h = self.lib.moe_b200_timer_create()
+
+    def run(self, x, out=None):
+        """moe_swarm_b200.run with per-stage events (same launches, same stream)."""
+        import moe_swarm_b200 as M
+        T, E, dev = M._validate(x["routing_logits"], x["routing_bias"], x["hidden_states"],
+                                x["hidden_states_scale"], x["gemm1_weights"], x["gemm1_weights_scale"],
+                                x["gemm2_weights"], x["gemm2_weights_scale"])
+        if out is None:
+            out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        buf = M._workspace(dev).get(T, E, stream)
+        a = M._args(T, E, x["routing_logits"], x["routing_bias"], x["hidden_states"],
+                    x["hidden_states_scale"], x["gemm1_weights"], x["gemm1_weights_scale"],
+                    x["gemm2_weights"], x["gemm2_weights_scale"], x["local_expert_offset"],
+                    x["routed_scaling_factor"], out)
+        rc = self.lib.moe_b200_forward_timed(ctypes.byref(a), buf.data_ptr(), buf.numel(), stream, self.h)
+        if rc != 0:
+            raise RuntimeError(f"moe_b200_forward_timed failed: {self.N.last_error()}")
+        return out
+
+    def read(self, reset=True):
+        ms = (ctypes.c_float * 3)()
+        calls = ctypes.c_int32()
+        rc = self.lib.moe_b200_timer_read(self.h, ms, ctypes.byref(calls), 1 if reset else 0)
+        if rc != 0:
+            raise RuntimeError(self.N.last_error())
+        return [float(v) for v in ms], int(calls.value)
+
+
+# ----------------------------------------------------------------------------- CPU baseline
+def cpu_sample(act_cpu, world, seed=0, k_experts=8, reps=1):
+    """Times the oracle port of reference/kernel_pytorch_v1.kernel on the host cores for the
+    first k experts of rank 0's shard, and scales by routed rows to the whole workload."""
+    from oracle import moe_ref as O
+    import moe_swarm_b200.workload as W
+    torch.set_num_threads(os.cpu_count() or 1)
+    T = act_cpu["routing_logits"].shape[0]
+    idx, w = O.route(act_cpu["routing_logits"], act_cpu["routing_bias"], 2.5)
+    total_rows = int(((idx >= 0) & (idx < E_GLOBAL)).sum())          # all 256 experts over all ranks
+    _, _, _, counts = O.local_permutation(idx, w, 0, E_GLOBAL)
+    # a contiguous block of k experts (a k-expert shard), the first one holding routed rows
+    lo = int((counts > 0).nonzero()[0]) if int(counts.sum()) else 0
+    lo = min(lo, E_GLOBAL - k_experts)
+    E = k_experts
+    x = dict(act_cpu)
+    x.update(W.make_weights(E, lo, seed))
+    x["local_expert_offset"] = lo
+    x["routed_scaling_factor"] = 2.5
+    sample_rows = int(sum(int(counts[e]) for e in range(lo, lo + E)))
+    O.run_v1(**x)                                                     # warm-up
+    best = None
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        O.run_v1(**x)
+        dt = time.perf_counter() - t0
+        best = dt if best is None else min(best, dt)
+    est = best * total_rows / max(1, sample_rows)
+    return {"value": T / est, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": (f"oracle port of reference/kernel_pytorch_v1.kernel on {E} local experts "
+                       f"[{lo},{lo + E}) holding {sample_rows} of {total_rows} routed rows at T={T}, "
+                       f"{best:.2f} s, scaled by routed rows to all 256 experts"),
+            "est_seconds_full": est}
+
+
+# ----------------------------------------------------------------------------- sweeps (N=1)
+def sweep(device, steps, peaks_):
+    import moe_swarm_b200 as M
+    import moe_swarm_b200.workload as W
+    out = []
+    weights = W.make_weights_fast(32, 7, device=device)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    timer = StageTimer()
+    fp8_peak = 2.0 * peaks_["bf16_tflops"]
+    for name, T, skew in [("decode", 1, 0.0), ("decode", 7, 0.0), ("decode", 16, 0.0), ("decode", 32, 0.0),
+                          ("decode", 64, 0.0), ("decode", 80, 0.0), ("mid_skewed", 901, 0.5),
+                          ("prefill", 8192, 0.0), ("prefill", 16384, 0.0)]:
+        x = {k: v.to(device) for k, v in W.make_activations(T, 1000 + T, skew=skew).items()}
+        x.update(weights)
+        x["local_expert_offset"] = 0
+        x["routed_scaling_factor"] = 2.5
+        f = routing_facts(x)
+        for _ in range(3):
+            M.run(**x)
+        n = max(5, min(steps, 30)) if T <= 1024 else max(3, min(steps, 10))
+        times = []
+        timer.read(reset=True)
+        for _ in range(n):
+            flush.zero_()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            timer.run(x)
+            e.record()
+            e.synchronize()
+            times.append(s.elapsed_time(e) * 1e3)
+        stage_ms, calls = timer.read(reset=True)
+        times.sort()
+        us = times[len(times) // 2]
+        g1, g2 = gemm_bytes(f)
+        byts = g1 + g2 + T * (256 * 4 + 56 * 4)
+        flops = f["rows"] * FLOP_PER_ASSIGN
+        rec = {"workload": name, "T": T, "active_experts": f["active"], "rows": f["rows"], "us": round(us, 1),
+               "tokens_per_s": round(T / (us * 1e-6), 1),
+               "stage_us": {k: round(v * 1e3 / calls, 1) for k, v in zip(("route", "gemm1", "gemm2"), stage_ms)},
+               "hbm_gbs": round(byts / (us * 1e-6) / 1e9, 1),
+               "hbm_frac": round(byts / (us * 1e-6) / 1e9 / peaks_["hbm_gbs"], 3),
+               "tflops": round(flops / (us * 1e-6) / 1e12, 1),
+               "fp8_frac": round(flops / (us * 1e-6) / 1e12 / fp8_peak, 3)}
+        out.append(rec)
+        del x
+    return out, {"fp8_peak_tflops": fp8_peak,
+                 "fp8_peak_source": "2x the measured cuBLAS bf16 burst peak (no measured fp8 peak)"}
+
+
+# ----------------------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-sweeps", action="store_true")
+    ap.add_argument("--cpu-experts", type=int, default=8)
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    steps, warmup = args.steps, max(3, args.warmup)
+
+    config = {"workload": "ep_full_layer_T4096 (benchmark config 4: 256 experts sharded 256/N per GPU)",
+              "T": EP_T, "experts_total": E_GLOBAL, "experts_per_gpu": E_GLOBAL // world,
+              "parallelism": f"ep{world}", "combine": "nccl reduce_scatter bf16" if world > 1 else "none",
+              "l2": "inputs larger than L2 (>=1.4 GB of routed weights per GPU per step)"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        import moe_swarm_b200.workload as W
+        act = W.make_activations(EP_T, 0)
+        vals = []
+        for i in range(max(1, steps)):
+            c = cpu_sample(act, world, k_experts=args.cpu_experts, reps=1)
+            vals.append(c)
+            if i + 1 >= min(steps, 3):
+                break
+        vals.sort(key=lambda c: c["value"])
+        c = vals[len(vals) // 2]
+        line = {"impl": "reference", "metric": METRIC, "value": round(c["value"], 2), "unit": "tokens/s",
+                "n_gpus": args.gpus, "steps": len(vals), "warmup": 1,
+                "ms_per_step": round(c["est_seconds_full"] * 1e3, 1), "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "bf16 (CPU)", "data": "synthetic",
+                "config": config,
+                "cpu_baseline": {k: c[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                "e2e": {"value": round(c["value"], 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    import moe_swarm_b200 as M
+    from moe_swarm_b200 import _native as N
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    pk = peaks()
+
+    x, act_cpu = ep_inputs(rank, world, device)
+    f = routing_facts(x)
+    T = EP_T
+    shard = torch.empty((T // world, H), dtype=torch.bfloat16, device=device)
+    timer = StageTimer()
+
+    def step(inp, use_timer):
+        out = timer.run(inp) if use_timer else M.run(**inp)
+        if world > 1:
+            dist.reduce_scatter_tensor(shard, out)
+            return shard
+        return out
+
+    for _ in range(warmup):
+        step(x, False)
+    torch.cuda.synchronize()
+    launches_per_step = N.lib().moe_b200_last_launch_count()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler()
+    if rank == 0:
+        clocks.start()
+    timer.read(reset=True)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        step(x, True)
+    end.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    stage_ms, calls = timer.read(reset=True)
+    visible = None
+    ck = clocks.stop(visible) if rank == 0 else None
+    t = torch.tensor([ms] + stage_ms, device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, stage_ms = float(t[0]), [float(v) for v in t[1:]]
+    ms_per_step = ms / steps
+
+    # e2e: host (pinned) activations -> device, layer, reduce-scatter, result -> host
+    names = ("routing_logits", "routing_bias", "hidden_states", "hidden_states_scale")
+    host = {k: act_cpu[k].contiguous().pin_memory() for k in names}
+    dev_in = {k: torch.empty_like(x[k]) for k in names}
+    xe = dict(x)
+    xe.update(dev_in)
+    res_host = torch.empty(shard.shape if world > 1 else (T, H), dtype=torch.bfloat16).pin_memory()
+    h2d = sum(v.numel() * v.element_size() for v in host.values())
+    d2h = res_host.numel() * res_host.element_size()
+
+    def e2e_step():
+        for k in names:
+            dev_in[k].copy_(host[k], non_blocking=True)
+        out = step(xe, False)
+        res_host.copy_(out, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for _ in range(steps):
+        e2e_step()
+    e2.record()
+    torch.cuda.synchronize()
+    te = torch.tensor([s2.elapsed_time(e2)], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_ms = float(te[0]) / steps
+
+    sweeps = None
+    cpu = None
+    if world == 1 and rank == 0:
+        if not args.no_sweeps:
+            sweeps, sweep_meta = sweep(device, steps, pk)
+        cpu = cpu_sample(act_cpu, world, k_experts=args.cpu_experts)
+
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    g1, g2 = gemm_bytes(f)
+    per_launch_ms = [v / steps for v in stage_ms]
+    dom = 1 if per_launch_ms[1] >= per_launch_ms[2] else 2
+    dom_bytes = g1 if dom == 1 else g2
+    dom_ms = per_launch_ms[dom]
+    achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
+    traffic = None
+    tf = ROOT / "profiles" / "traffic.json"
+    if tf.exists():
+        try:
+            traffic = json.loads(tf.read_text()).get(f"ep{world}_gemm{dom}")
+        except ValueError:
+            traffic = None
+    line = {
+        "metric": METRIC,
+        "value": round(T / (ms_per_step * 1e-3), 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": steps,
+        "warmup": warmup,
+        "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "fp8 e4m3 x e4m3 -> fp32 (bf16 out)",
+        "data": "synthetic (seeded activations; random-init weights on the device)",
+        "config": config,
+        "latency_us": round(ms_per_step * 1e3, 1),
+        "stage_us": {k: round(v * 1e3, 1) for k, v in zip(("route", "gemm1", "gemm2"), per_launch_ms)},
+        "routing": {"active_experts_rank0": f["active"], "rows_rank0": f["rows"]},
+        "roofline": {"kernel": f"gemm_kernel<{dom}>", "bound": "hbm", "achieved": round(achieved, 1),
+                     "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 3),
+                     "traffic": traffic, "algorithmic_bytes_per_launch": dom_bytes,
+                     "peak_source": pk["source"] + " (MEASURED_PEAKS.json hbm_gbs, burst copy)"},
+        "e2e": {"value": round(T / (e2e_ms * 1e-3), 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4)},
+        "gpu_launches": launches_per_step * steps,
+        "clocks": ck,
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = {k: (round(v, 3) if isinstance(v, float) else v) for k, v in cpu.items()
+                                if k in ("value", "unit", "cores", "kind", "sample")}
+    if sweeps is not None:
+        line["sweeps"] = sweeps
+        line["sweep_meta"] = sweep_meta
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -146,6 +146,23 @@ MOE_B200_API int moe_b200_route(const moe_b200_args* args, void* workspace, size
 MOE_B200_API int moe_b200_device_status(void* workspace, size_t workspace_bytes, int32_t num_tokens,
                            int32_t num_local_experts, void* stream, int32_t clear);
 
+/*
+ * Per-stage device timing for benchmarks.  A timer records CUDA events on the
+ * call's stream between the stages of moe_b200_forward_timed (routing +
+ * permutation, GEMM1, GEMM2) and accumulates their durations; reading it
+ * synchronises on the last recorded event.  Up to 4096 calls are held between
+ * reads.  Timing adds two event records per stage and nothing else.
+ */
+typedef struct moe_b200_timer moe_b200_timer;
+MOE_B200_API moe_b200_timer* moe_b200_timer_create(void);
+MOE_B200_API void moe_b200_timer_destroy(moe_b200_timer* timer);
+MOE_B200_API int moe_b200_forward_timed(const moe_b200_args* args, void* workspace,
+                                        size_t workspace_bytes, void* stream, moe_b200_timer* timer);
+/* stage_ms[3] = summed milliseconds of {routing+permutation, GEMM1, GEMM2}; *calls = calls
+ * summed; with `reset` != 0 the timer is emptied.  Returns a status code. */
+MOE_B200_API int moe_b200_timer_read(moe_b200_timer* timer, float* stage_ms, int32_t* calls,
+                                     int32_t reset);
+
 /* Text of the last host-side error of this thread ("" if none). */
 MOE_B200_API const char* moe_b200_last_error(void);
 

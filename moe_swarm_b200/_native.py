@@ -26,6 +26,10 @@ EXPORTED = (
     "moe_b200_device_status",
     "moe_b200_last_error",
     "moe_b200_last_launch_count",
+    "moe_b200_timer_create",
+    "moe_b200_timer_destroy",
+    "moe_b200_forward_timed",
+    "moe_b200_timer_read",
 )
 
 
@@ -83,6 +87,14 @@ def lib() -> ctypes.CDLL:
     l.moe_b200_last_error.restype = ctypes.c_char_p
     l.moe_b200_last_launch_count.argtypes = []
     l.moe_b200_last_launch_count.restype = ctypes.c_int
+    l.moe_b200_timer_create.argtypes = []
+    l.moe_b200_timer_create.restype = vp
+    l.moe_b200_timer_destroy.argtypes = [vp]
+    l.moe_b200_timer_destroy.restype = None
+    l.moe_b200_forward_timed.argtypes = [ctypes.POINTER(MoeArgs), vp, sz, vp, vp]
+    l.moe_b200_forward_timed.restype = ctypes.c_int
+    l.moe_b200_timer_read.argtypes = [vp, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_int32), i32]
+    l.moe_b200_timer_read.restype = ctypes.c_int
     _lib = l
     return l
 

@@ -8,6 +8,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "../../include/moe_b200.h"
 #include "launch_args.cuh"
@@ -217,7 +218,21 @@ int moe_b200_route(const moe_b200_args* a, void* workspace, size_t ws_bytes, voi
                       static_cast<cudaStream_t>(stream), &launches);
 }
 
-int moe_b200_forward(const moe_b200_args* a, void* workspace, size_t ws_bytes, void* stream) {
+}  // extern "C"
+
+struct moe_b200_timer {
+  std::vector<cudaEvent_t> ev;   // 4 events per call: start, after routing, after GEMM1, after GEMM2
+  int used = 0;
+  static constexpr int kCap = 4096;
+  ~moe_b200_timer() {
+    for (cudaEvent_t e : ev) cudaEventDestroy(e);
+  }
+};
+
+namespace {
+
+int forward_impl(const moe_b200_args* a, void* workspace, size_t ws_bytes, void* stream,
+                 moe_b200_timer* timer) {
   g_last_launches = 0;
   moe::Layout L;
   int dev = 0;
@@ -232,9 +247,23 @@ int moe_b200_forward(const moe_b200_args* a, void* workspace, size_t ws_bytes, v
     if (e1 != cudaSuccess) return cuda_fail(e1, "cudaFuncSetAttribute(gemm)");
     di.smem_set = true;
   }
+  cudaEvent_t* ev = nullptr;
+  if (timer) {
+    if (timer->used >= moe_b200_timer::kCap) return fail(MOE_B200_ERR_ARG, "timer full: read it with reset");
+    while ((int)timer->ev.size() < 4 * (timer->used + 1)) {
+      cudaEvent_t e;
+      cudaError_t ce = cudaEventCreate(&e);
+      if (ce != cudaSuccess) return cuda_fail(ce, "cudaEventCreate");
+      timer->ev.push_back(e);
+    }
+    ev = timer->ev.data() + 4 * timer->used;
+    ++timer->used;
+    cudaEventRecord(ev[0], st);
+  }
   int launches = 0;
   rc = launch_route(a, ws, L, di.sms, st, &launches);
   if (rc) return rc;
+  if (ev) cudaEventRecord(ev[1], st);
 
   const int E = a->num_local_experts;
   CUtensorMap mA1, mW13, mChi, mClo, mW2;
@@ -273,6 +302,7 @@ int moe_b200_forward(const moe_b200_args* a, void* workspace, size_t ws_bytes, v
   cudaError_t e = moe::gemm_launch(1, di.sms, st, mA1, mA1, mW13, g1);
   if (e != cudaSuccess) return cuda_fail(e, "gemm1 launch");
   ++launches;
+  if (ev) cudaEventRecord(ev[2], st);
   moe::GemmArgs g2 = g;
   g2.e_ustart = reinterpret_cast<const int*>(ws + L.e_u2);
   g2.sa = reinterpret_cast<const float*>(ws + L.c_scale);
@@ -280,7 +310,45 @@ int moe_b200_forward(const moe_b200_args* a, void* workspace, size_t ws_bytes, v
   e = moe::gemm_launch(2, di.sms, st, mChi, mClo, mW2, g2);
   if (e != cudaSuccess) return cuda_fail(e, "gemm2 launch");
   ++launches;
+  if (ev) cudaEventRecord(ev[3], st);
   g_last_launches = launches;
+  return MOE_B200_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int moe_b200_forward(const moe_b200_args* a, void* workspace, size_t ws_bytes, void* stream) {
+  return forward_impl(a, workspace, ws_bytes, stream, nullptr);
+}
+
+moe_b200_timer* moe_b200_timer_create(void) { return new moe_b200_timer(); }
+
+void moe_b200_timer_destroy(moe_b200_timer* t) { delete t; }
+
+int moe_b200_forward_timed(const moe_b200_args* a, void* workspace, size_t ws_bytes, void* stream,
+                           moe_b200_timer* timer) {
+  if (!timer) return fail(MOE_B200_ERR_ARG, "null timer");
+  return forward_impl(a, workspace, ws_bytes, stream, timer);
+}
+
+int moe_b200_timer_read(moe_b200_timer* t, float* stage_ms, int32_t* calls, int32_t reset) {
+  if (!t || !stage_ms || !calls) return fail(MOE_B200_ERR_ARG, "null argument");
+  stage_ms[0] = stage_ms[1] = stage_ms[2] = 0.f;
+  *calls = t->used;
+  if (t->used > 0) {
+    cudaError_t e = cudaEventSynchronize(t->ev[4 * (t->used - 1) + 3]);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaEventSynchronize");
+    for (int i = 0; i < t->used; ++i)
+      for (int s = 0; s < 3; ++s) {
+        float ms = 0.f;
+        e = cudaEventElapsedTime(&ms, t->ev[4 * i + s], t->ev[4 * i + s + 1]);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaEventElapsedTime");
+        stage_ms[s] += ms;
+      }
+  }
+  if (reset) t->used = 0;
   return MOE_B200_OK;
 }
 

@@ -77,8 +77,11 @@ def test_layer_matches_reference_golden(cuda_device, path):
     torch.cuda.synchronize()
     _status_ok(cuda_device)
     _expect_parity(out, g["official"], "vs reference_official")
-    # v1 (bf16 dequantised GEMMs) is itself up to ~0.1% of elements off the official output
-    _expect_parity(out, g["v1"], "vs kernel_pytorch_v1", max_bad=out.numel() // 500)
+    # kernel_pytorch_v1 (bf16-dequantised GEMMs) is itself off the official output on up to
+    # ~2% of elements at this tolerance (971 of 57344 in the steered case), so against v1 the
+    # bar is: no further from v1 than the official reference is.
+    v1_vs_official = O.parity_report(g["v1"], g["official"], atol=C.ATOL, rtol=C.RTOL)["bad"]
+    _expect_parity(out, g["v1"], "vs kernel_pytorch_v1", max_bad=int(1.25 * v1_vs_official) + 16)
 
 
 def _intermediate_check(d, x, device):
