@@ -101,6 +101,7 @@ typedef struct moe_b200_layout {
   size_t c_lo;        /* e4m3  [R, 2048]: SwiGLU output, residual x16 */
   size_t c_scale;     /* f32   [16, r_pad]: per-(row, 128-block) scale of c_hi */
   size_t status;      /* int32: device status word (0 = ok) */
+  size_t trace;       /* uint64 [4 kernels][256 CTAs][16]: per-CTA counters of a traced build */
   size_t r_max;       /* rows reserved: T * min(8, E_local) */
   size_t r_pad;       /* leading dimension of the [blocks, rows] scale arrays */
   size_t total;       /* bytes */

@@ -8,7 +8,10 @@ from __future__ import annotations
 import ctypes
 from pathlib import Path
 
-LIB_PATH = Path(__file__).resolve().with_name("libmoe_b200.so")
+import os
+
+# MOE_B200_LIB selects another build of the library (e.g. the MOE_TRACE build).
+LIB_PATH = Path(os.environ.get("MOE_B200_LIB") or Path(__file__).resolve().with_name("libmoe_b200.so"))
 
 OK = 0
 ERR_ARG = 1
@@ -54,7 +57,7 @@ class MoeArgs(ctypes.Structure):
 class MoeLayout(ctypes.Structure):
     _fields_ = [(name, ctypes.c_size_t) for name in (
         "plan", "topk_idx", "topk_w", "tok_nloc", "tok_rows", "e_count", "e_start", "row_token",
-        "row_weight", "c_hi", "c_lo", "c_scale", "status", "r_max", "r_pad", "total")]
+        "row_weight", "c_hi", "c_lo", "c_scale", "status", "trace", "r_max", "r_pad", "total")]
 
 
 _lib = None

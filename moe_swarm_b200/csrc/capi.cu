@@ -17,9 +17,12 @@
 namespace moe {
 
 cudaError_t route_launch(const RouteArgs& a, cudaStream_t st, int* launches);
-cudaError_t gemm_prepare();
-cudaError_t gemm_launch(int mode, int grid, cudaStream_t st, const CUtensorMap& a, const CUtensorMap& a2,
-                        const CUtensorMap& b, const GemmArgs& g);
+cudaError_t wide_prepare();
+cudaError_t wide_launch(int mode, int grid, cudaStream_t st, const CUtensorMap& a, const CUtensorMap& a2,
+                        const CUtensorMap& b, const TileArgs& g);
+cudaError_t stream_prepare();
+cudaError_t stream_launch(int mode, int grid, cudaStream_t st, const CUtensorMap& w, const CUtensorMap& t,
+                          const CUtensorMap& t2, const TileArgs& g);
 
 }  // namespace moe
 
@@ -56,12 +59,12 @@ EncodeTiledFn encode_fn() {
 }
 
 // Byte matrix [rows, cols] (row stride = cols bytes) read as 128x128-byte tiles, SWIZZLE_128B.
-bool encode_u8_2d(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows) {
+bool encode_u8_2d(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, uint32_t box_rows = 128) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   const cuuint64_t dims[2] = {cols, rows};
   const cuuint64_t strides[1] = {cols};
-  const cuuint32_t box[2] = {128, 128};
+  const cuuint32_t box[2] = {128, box_rows};
   const cuuint32_t estr[2] = {1, 1};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -133,6 +136,8 @@ moe::RouteArgs make_route_args(const moe_b200_args* a, uint8_t* ws, const moe::L
   r.e_mt_start = reinterpret_cast<int*>(ws + L.e_mt_start);
   r.e_u1 = reinterpret_cast<int*>(ws + L.e_u1);
   r.e_u2 = reinterpret_cast<int*>(ws + L.e_u2);
+  r.e_tt = reinterpret_cast<int*>(ws + L.e_tt);
+  r.e_m64 = reinterpret_cast<int*>(ws + L.e_m64);
   r.row_token = reinterpret_cast<int*>(ws + L.row_token);
   r.row_weight = reinterpret_cast<float*>(ws + L.row_weight);
   r.a_perm = ws + L.a_perm;
@@ -190,6 +195,7 @@ int moe_b200_workspace_layout(int32_t num_tokens, int32_t num_local_experts, moe
   out->c_lo = L.c_lo;
   out->c_scale = L.c_scale;
   out->status = L.status;
+  out->trace = L.trace;
   out->r_max = L.r_max;
   out->r_pad = L.r_pad;
   out->total = L.total;
@@ -231,6 +237,29 @@ struct moe_b200_timer {
 
 namespace {
 
+moe::TileArgs tile_args(const moe_b200_args* a, uint8_t* ws, const moe::Layout& L) {
+  moe::TileArgs s{};
+  s.plan = reinterpret_cast<const moe::Plan*>(ws + L.plan);
+  s.e_count = reinterpret_cast<const int*>(ws + L.e_count);
+  s.e_start = reinterpret_cast<const int*>(ws + L.e_start);
+  s.E = a->num_local_experts;
+  s.r_pad = L.r_pad;
+  s.c_hi = ws + L.c_hi;
+  s.c_lo = ws + L.c_lo;
+  s.c_scale = reinterpret_cast<float*>(ws + L.c_scale);
+  s.part = reinterpret_cast<float*>(ws + L.sk_part);
+  s.tile_cnt = reinterpret_cast<int*>(ws + L.sk_cnt);
+  s.row_token = reinterpret_cast<const int*>(ws + L.row_token);
+  s.row_weight = reinterpret_cast<const float*>(ws + L.row_weight);
+  s.tok_nloc = reinterpret_cast<const int*>(ws + L.tok_nloc);
+  s.tok_rows = reinterpret_cast<const int*>(ws + L.tok_rows);
+  s.part2 = reinterpret_cast<float*>(ws + L.part2);
+  s.cnt2 = reinterpret_cast<int*>(ws + L.cnt2);
+  s.out = a->output;
+  s.status = reinterpret_cast<int*>(ws + L.status);
+  return s;
+}
+
 int forward_impl(const moe_b200_args* a, void* workspace, size_t ws_bytes, void* stream,
                  moe_b200_timer* timer) {
   g_last_launches = 0;
@@ -243,8 +272,10 @@ int forward_impl(const moe_b200_args* a, void* workspace, size_t ws_bytes, void*
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   if (!di.smem_set) {
-    cudaError_t e1 = moe::gemm_prepare();
-    if (e1 != cudaSuccess) return cuda_fail(e1, "cudaFuncSetAttribute(gemm)");
+    cudaError_t e1 = moe::wide_prepare();
+    if (e1 != cudaSuccess) return cuda_fail(e1, "cudaFuncSetAttribute(wide)");
+    e1 = moe::stream_prepare();
+    if (e1 != cudaSuccess) return cuda_fail(e1, "cudaFuncSetAttribute(stream)");
     di.smem_set = true;
   }
   cudaEvent_t* ev = nullptr;
@@ -266,49 +297,64 @@ int forward_impl(const moe_b200_args* a, void* workspace, size_t ws_bytes, void*
   if (ev) cudaEventRecord(ev[1], st);
 
   const int E = a->num_local_experts;
+  if (a->num_tokens <= moe::kStreamMaxT) {
+    CUtensorMap mTok, mW13s, mHi, mLo, mW2s;
+    if (!encode_u8_2d(&mTok, ws + L.a_perm, moe::kH, L.r_pad, moe::kTok) ||
+        !encode_u8_2d(&mW13s, a->gemm1_weights, moe::kH, (uint64_t)E * moe::kN1) ||
+        !encode_u8_2d(&mHi, ws + L.c_hi, moe::kI, L.r_pad, moe::kTok) ||
+        !encode_u8_2d(&mLo, ws + L.c_lo, moe::kI, L.r_pad, moe::kTok) ||
+        !encode_u8_2d(&mW2s, a->gemm2_weights, moe::kI, (uint64_t)E * moe::kH))
+      return fail(MOE_B200_ERR_CUDA, "cuTensorMapEncodeTiled failed");
+    moe::TileArgs s = tile_args(a, ws, L);
+    s.e_tiles = reinterpret_cast<const int*>(ws + L.e_tt);
+    unsigned long long* trace = reinterpret_cast<unsigned long long*>(ws + L.trace);
+    const int grid = di.sms < moe::kMaxSms ? di.sms : moe::kMaxSms;
+    moe::TileArgs s1 = s;
+    s1.sa = reinterpret_cast<const float*>(ws + L.sa_perm);
+    s1.sw = a->gemm1_weights_scale;
+    s1.trace = trace;
+    cudaError_t e = moe::stream_launch(1, grid, st, mW13s, mTok, mTok, s1);
+    if (e != cudaSuccess) return cuda_fail(e, "stream gemm1 launch");
+    ++launches;
+    if (ev) cudaEventRecord(ev[2], st);
+    moe::TileArgs s2 = s;
+    s2.sa = reinterpret_cast<const float*>(ws + L.c_scale);
+    s2.sw = a->gemm2_weights_scale;
+    s2.trace = trace + (size_t)moe::kMaxSms * moe::kTraceSlots;
+    e = moe::stream_launch(2, grid, st, mW2s, mHi, mLo, s2);
+    if (e != cudaSuccess) return cuda_fail(e, "stream gemm2 launch");
+    ++launches;
+    if (ev) cudaEventRecord(ev[3], st);
+    g_last_launches = launches;
+    return MOE_B200_OK;
+  }
+  // wide (token-major) kernels for large T
   CUtensorMap mA1, mW13, mChi, mClo, mW2;
-  if (!encode_u8_2d(&mA1, ws + L.a_perm, moe::kH, L.r_pad) ||
+  if (!encode_u8_2d(&mA1, ws + L.a_perm, moe::kH, L.r_pad, 128) ||
       !encode_u8_2d(&mW13, a->gemm1_weights, moe::kH, (uint64_t)E * moe::kN1) ||
-      !encode_u8_2d(&mChi, ws + L.c_hi, moe::kI, L.r_pad) || !encode_u8_2d(&mClo, ws + L.c_lo, moe::kI, L.r_pad) ||
+      !encode_u8_2d(&mChi, ws + L.c_hi, moe::kI, L.r_pad, 16) ||
+      !encode_u8_2d(&mClo, ws + L.c_lo, moe::kI, L.r_pad, 16) ||
       !encode_u8_2d(&mW2, a->gemm2_weights, moe::kI, (uint64_t)E * moe::kH))
     return fail(MOE_B200_ERR_CUDA, "cuTensorMapEncodeTiled failed");
-
-  moe::GemmArgs g{};
-  g.plan = reinterpret_cast<const moe::Plan*>(ws + L.plan);
-  g.e_count = reinterpret_cast<const int*>(ws + L.e_count);
-  g.e_start = reinterpret_cast<const int*>(ws + L.e_start);
-  g.e_mt_start = reinterpret_cast<const int*>(ws + L.e_mt_start);
-  g.E = E;
-  g.r_split = static_cast<int>(L.r_max < (size_t)moe::kRSplit ? L.r_max : (size_t)moe::kRSplit);
-  g.r_pad = L.r_pad;
-  g.c_hi = ws + L.c_hi;
-  g.c_lo = ws + L.c_lo;
-  g.c_scale = reinterpret_cast<float*>(ws + L.c_scale);
-  g.part1 = reinterpret_cast<float*>(ws + L.part1);
-  g.cnt1 = reinterpret_cast<int*>(ws + L.cnt1);
-  g.row_token = reinterpret_cast<const int*>(ws + L.row_token);
-  g.row_weight = reinterpret_cast<const float*>(ws + L.row_weight);
-  g.tok_nloc = reinterpret_cast<const int*>(ws + L.tok_nloc);
-  g.tok_rows = reinterpret_cast<const int*>(ws + L.tok_rows);
-  g.part2 = reinterpret_cast<float*>(ws + L.part2);
-  g.cnt2 = reinterpret_cast<int*>(ws + L.cnt2);
-  g.out = a->output;
-  g.status = reinterpret_cast<int*>(ws + L.status);
-
-  moe::GemmArgs g1 = g;
-  g1.e_ustart = reinterpret_cast<const int*>(ws + L.e_u1);
-  g1.sa = reinterpret_cast<const float*>(ws + L.sa_perm);
-  g1.sw = a->gemm1_weights_scale;
-  cudaError_t e = moe::gemm_launch(1, di.sms, st, mA1, mA1, mW13, g1);
-  if (e != cudaSuccess) return cuda_fail(e, "gemm1 launch");
+  moe::TileArgs w = tile_args(a, ws, L);
+  unsigned long long* trace = reinterpret_cast<unsigned long long*>(ws + L.trace);
+  const int grid = di.sms < moe::kMaxSms ? di.sms : moe::kMaxSms;
+  moe::TileArgs w1 = w;
+  w1.e_tiles = reinterpret_cast<const int*>(ws + L.e_mt_start);
+  w1.sa = reinterpret_cast<const float*>(ws + L.sa_perm);
+  w1.sw = a->gemm1_weights_scale;
+  w1.trace = trace + 2 * (size_t)moe::kMaxSms * moe::kTraceSlots;
+  cudaError_t e = moe::wide_launch(1, grid, st, mA1, mA1, mW13, w1);
+  if (e != cudaSuccess) return cuda_fail(e, "wide gemm1 launch");
   ++launches;
   if (ev) cudaEventRecord(ev[2], st);
-  moe::GemmArgs g2 = g;
-  g2.e_ustart = reinterpret_cast<const int*>(ws + L.e_u2);
-  g2.sa = reinterpret_cast<const float*>(ws + L.c_scale);
-  g2.sw = a->gemm2_weights_scale;
-  e = moe::gemm_launch(2, di.sms, st, mChi, mClo, mW2, g2);
-  if (e != cudaSuccess) return cuda_fail(e, "gemm2 launch");
+  moe::TileArgs w2 = w;
+  w2.e_tiles = reinterpret_cast<const int*>(ws + L.e_m64);
+  w2.sa = reinterpret_cast<const float*>(ws + L.c_scale);
+  w2.sw = a->gemm2_weights_scale;
+  w2.trace = trace + 3 * (size_t)moe::kMaxSms * moe::kTraceSlots;
+  e = moe::wide_launch(2, grid, st, mChi, mClo, mW2, w2);
+  if (e != cudaSuccess) return cuda_fail(e, "wide gemm2 launch");
   ++launches;
   if (ev) cudaEventRecord(ev[3], st);
   g_last_launches = launches;

@@ -33,30 +33,30 @@ struct RouteArgs {
   int* e_mt_start;
   int* e_u1;
   int* e_u2;
+  int* e_tt;
+  int* e_m64;
   int* row_token;
   float* row_weight;
   uint8_t* a_perm;
   float* sa_perm;
 };
 
-struct GemmArgs {
+
+// Arguments of the grouped-GEMM kernels (streaming and wide variants, both modes).
+struct TileArgs {
   const Plan* plan;
   const int* e_count;
   const int* e_start;
-  const int* e_mt_start;
-  const int* e_ustart;
+  const int* e_tiles;   // per-expert prefix of this kernel's token tiles (E + 1 entries)
   int E;
-  int r_split;
   size_t r_pad;
-  const float* sa;   // MODE1: activation scales [56][r_pad]; MODE2: C scales [16][r_pad]
-  const float* sw;   // MODE1: gemm1_weights_scale [E][32][56]; MODE2: gemm2_weights_scale [E][56][16]
-  // MODE1 outputs
+  const float* sa;   // MODE 1: activation scales [56][r_pad]; MODE 2: C scales [16][r_pad]
+  const float* sw;   // MODE 1: gemm1_weights_scale [E][32][56]; MODE 2: gemm2_weights_scale [E][56][16]
   uint8_t* c_hi;
   uint8_t* c_lo;
   float* c_scale;
-  float* part1;
-  int* cnt1;
-  // MODE2
+  float* part;       // stream-K partial slots
+  int* tile_cnt;     // stream-K per-tile arrival counters (self-resetting)
   const int* row_token;
   const float* row_weight;
   const int* tok_nloc;
@@ -65,29 +65,10 @@ struct GemmArgs {
   int* cnt2;
   uint16_t* out;
   int* status;
+  unsigned long long* trace;   // [kMaxSms][kTraceSlots] of this kernel (written by MOE_TRACE builds)
 };
 
-constexpr int kStages = 4;
-constexpr int kTileBytes = 128 * 128;
-constexpr int kStageBytes = 3 * kTileBytes;
-constexpr int kGemmThreads = 320;
-constexpr int kEpiWarps = 8;
-constexpr int kEpiThreads = kEpiWarps * 32;
 
-struct GemmSmem {
-  uint8_t tiles[kStages][3][kTileBytes];
-  uint64_t full[kStages];
-  uint64_t empty[kStages];
-  uint64_t tfull[2];
-  uint64_t tempty[2];
-  uint64_t drain;
-  uint32_t tmem_base;
-  int abort;
-  int last_flag;
-  int pad;
-  float amax[2][128];
-};
 
-constexpr size_t kGemmSmemBytes = sizeof(GemmSmem) + 1024;
 
 }  // namespace moe

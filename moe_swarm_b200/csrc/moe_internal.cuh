@@ -19,8 +19,14 @@ constexpr int kKB2 = kI / kBlk;   // 16 K-blocks of GEMM2
 constexpr int kNT1 = kI / kBlk;   // 16 GEMM1 tiles (128 X1 + 128 X2 rows each)
 constexpr int kNT2 = kH / kBlk;   // 56 GEMM2 tiles (128 output features each)
 
-constexpr int kChunk = 128;       // tokens per routing CTA
-constexpr int kRouteThreads = 512;
+constexpr int kChunk = 128;       // tokens per rank-mask chunk of the permutation
+constexpr int kRouteWarps = 8;    // routing / scatter CTAs: one token per warp
+constexpr int kRouteThreads = kRouteWarps * 32;
+constexpr int kTok = 32;          // token tile (MMA N) of the streaming kernels
+constexpr int kMaxSms = 256;      // partial-slot capacity of the stream-K fixup (2 per CTA)
+constexpr int kStreamMaxT = 512;
+constexpr int kTraceSlots = 16;   // per-CTA counters of a traced build (MOE_TRACE)
+constexpr int kTraceKernels = 4;  // stream GEMM1, stream GEMM2, wide GEMM1, wide GEMM2  // T above which the wide (token-major) kernels run
 constexpr int kRSplit = 256;      // split-K is considered only when rows <= kRSplit
 constexpr int kS1Max = 14;        // GEMM1 split factors: divisors of 56 up to 14
 constexpr int kS2Max = 8;         // GEMM2 split factors: divisors of 16 up to 8
@@ -38,9 +44,11 @@ enum : int {
 // Written by the routing scan, read by the GEMM kernels.
 struct Plan {
   int T, E, rows, m_tiles;
-  int s1, kb1, units1;    // GEMM1 split factor, K-blocks per split, work units
-  int s2, kb2, units2;    // GEMM2
-  int pad[6];
+  int s1, kb1, units1;    // wide GEMM1 split factor, K-blocks per split, work units
+  int s2, kb2, units2;    // wide GEMM2
+  int tt;                 // 32-row token tiles (streaming kernels)
+  int m64;                // 64-row token tiles
+  int pad[4];
 };
 
 struct Layout {
@@ -50,7 +58,8 @@ struct Layout {
   size_t plan, route_done, status;
   size_t topk_idx, topk_w, tok_nloc, tok_le, tok_lw, tok_rows;
   size_t chunk_hist, chunk_base;
-  size_t e_count, e_start, e_mt_start, e_u1, e_u2;
+  size_t e_count, e_start, e_mt_start, e_u1, e_u2, e_tt, e_m64;
+  size_t sk_part, sk_cnt, trace;
   size_t row_token, row_weight;
   size_t a_perm, sa_perm;
   size_t c_hi, c_lo, c_scale;
@@ -86,6 +95,8 @@ inline bool compute_layout(int T, int E, Layout* L) {
   l.status = take(sizeof(int));
   l.cnt1 = take(l.mt_max * kNT1 * sizeof(int));
   l.cnt2 = take(tt * kNT2 * 2 * sizeof(int));
+  l.chunk_hist = take((size_t)(l.nchunks > 0 ? l.nchunks : 1) * E * sizeof(int));
+  l.sk_cnt = take(((l.r_max + kTok - 1) / kTok + E) * kNT2 * sizeof(int));
   l.counters_end = align_up(o, 1024);
   l.topk_idx = take(tt * kTopK * sizeof(int));
   l.topk_w = take(tt * kTopK * sizeof(float));
@@ -93,13 +104,14 @@ inline bool compute_layout(int T, int E, Layout* L) {
   l.tok_le = take(tt * kTopK * sizeof(int));
   l.tok_lw = take(tt * kTopK * sizeof(float));
   l.tok_rows = take(tt * kTopK * sizeof(int));
-  l.chunk_hist = take((size_t)(l.nchunks > 0 ? l.nchunks : 1) * E * sizeof(int));
   l.chunk_base = take((size_t)(l.nchunks > 0 ? l.nchunks : 1) * E * sizeof(int));
   l.e_count = take((size_t)E * sizeof(int));
   l.e_start = take((size_t)(E + 1) * sizeof(int));
   l.e_mt_start = take((size_t)(E + 1) * sizeof(int));
   l.e_u1 = take((size_t)(E + 1) * sizeof(int));
   l.e_u2 = take((size_t)(E + 1) * sizeof(int));
+  l.e_tt = take((size_t)(E + 1) * sizeof(int));
+  l.e_m64 = take((size_t)(E + 1) * sizeof(int));
   l.row_token = take(l.r_pad * sizeof(int));
   l.row_weight = take(l.r_pad * sizeof(float));
   l.a_perm = take(l.r_pad * kH);
@@ -110,6 +122,8 @@ inline bool compute_layout(int T, int E, Layout* L) {
   l.part1 = take((size_t)kS1Max * r_split * kN1 * sizeof(float));
   const size_t p2_rows = l.r_pad > (size_t)kS2Max * r_split ? l.r_pad : (size_t)kS2Max * r_split;
   l.part2 = take(p2_rows * kH * sizeof(float));
+  l.sk_part = take((size_t)2 * kMaxSms * 128 * 256 * sizeof(float));
+  l.trace = take((size_t)kTraceKernels * kMaxSms * kTraceSlots * sizeof(unsigned long long));
   l.total = align_up(o, 1024);
   *L = l;
   return true;

@@ -221,6 +221,43 @@ __device__ __forceinline__ uint64_t sdesc_k128_sw128(uint32_t smem_addr) {
   return d;
 }
 
+// ---------------------------------------------------------------- inter-CTA arrival
+// Arrival on a global counter with acquire-release semantics at GPU scope.  Used after a
+// CTA barrier by one thread, it publishes every store the CTA made before the barrier
+// (release is cumulative over what the barrier made visible) and, for the last arriver,
+// acquires the other CTAs' published stores.
+__device__ __forceinline__ int atomic_add_acq_rel_gpu(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
+// ---------------------------------------------------------------- programmatic dependent launch
+// Wait until the preceding kernel in the stream has completed and its writes are visible
+// (a no-op when the kernel was not launched as a programmatic dependent).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Allow the next kernel in the stream (launched as a programmatic dependent) to start its
+// prologue on SMs this grid frees; it still waits for this grid's completion before
+// reading anything this grid writes.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Max over the 32 lanes of each of 32 columns: on entry v[c] is this lane's value of column
+// c; on exit v[0] is the max of column `lane` over the warp (31 shuffles, transpose-reduce).
+__device__ __forceinline__ void warp_colmax32(float* v, int lane) {
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    const bool upper = (lane & off) != 0;
+#pragma unroll
+    for (int i = 0; i < off; ++i) {
+      const float send = upper ? v[i] : v[i + off];
+      const float keep = upper ? v[i + off] : v[i];
+      v[i] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, off));
+    }
+  }
+}
+
 // ---------------------------------------------------------------- misc
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");

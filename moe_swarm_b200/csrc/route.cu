@@ -1,22 +1,22 @@
-// DeepSeek-V3 no-aux routing fused with the token->expert histogram, the
-// prefix sum and the permutation of activation rows into expert-major order.
+// DeepSeek-V3 no-aux routing fused with the token->expert histogram, the prefix sums
+// (expert segments and GEMM tile tables) and the permutation of activation rows into
+// expert-major order.
 //
-// Semantics follow spec/reference_official.py:95-126 (selection on
-// sigmoid(logits)+bias, 8 groups scored by their top-2 sum, 4 groups kept,
-// top-8 experts, bias-free weights normalised then scaled) and the row order
-// of reference/kernel_pytorch_v1.py:100-123 (stable sort by local expert:
-// expert-major, token-minor).  The reference's Triton kernel appends picks to
-// per-expert buckets with atomics (solution/python/kernel.py:137-213), which
-// makes the row order run-dependent; here every row index is a prefix count,
-// so the permutation is deterministic and identical to the oracle's.
+// Semantics follow spec/reference_official.py:95-126 (selection on sigmoid(logits)+bias,
+// 8 groups scored by their top-2 sum, 4 groups kept, top-8 experts, bias-free weights
+// normalised then scaled) and the row order of reference/kernel_pytorch_v1.py:100-123
+// (stable sort by local expert: expert-major, token-minor).  The reference's Triton kernel
+// appends picks to per-expert buckets with atomics (solution/python/kernel.py:137-213),
+// which makes the row order run-dependent; here every row index is a prefix count, so the
+// permutation is deterministic and identical to the oracle's.
 //
-// Work split: one warp per token; lane l owns experts 8l..8l+7, so the four
-// lanes 4g..4g+3 own group g.  A CTA routes a chunk of 128 tokens and keeps
-// per-expert token bitmasks of its chunk in shared memory; the rank of a token
-// inside an expert's segment is a popcount over those masks plus the chunk's
-// base.  With one chunk (T <= 128, the decode regime) a single CTA does
-// routing, scan and scatter in one launch; otherwise the last CTA to finish
-// routing performs the scan and a second kernel scatters.
+// route_kernel: one warp per token (lane l owns experts 8l..8l+7, the four lanes 4g..4g+3
+// own group g), 8 tokens per CTA.  Local picks are counted per 128-token chunk with global
+// atomics (order-independent sums).  The last CTA to finish (a self-resetting arrival
+// counter) turns the chunk counts into expert segment starts, per-chunk bases and the GEMM
+// tile tables (plan), zeroes the counts for the next call, and, when T <= 128, performs the
+// permutation itself.  scatter_kernel (T > 128): 8 tokens per CTA; the rank of a token in an
+// expert's segment is a popcount over the chunk's per-expert token bitmask plus the chunk base.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -25,7 +25,6 @@
 #include "ptx.cuh"
 
 namespace moe {
-
 
 __device__ __forceinline__ uint32_t orderable(float v) {
   uint32_t u = __float_as_uint(v);
@@ -46,9 +45,10 @@ __device__ __forceinline__ int warp_excl_prefix(int v, int lane) {
   return x - v;
 }
 
-// Routes token t with the calling warp; records it in the chunk's histogram and masks.
-__device__ void route_token(const RouteArgs& a, const float* s_bias, int t, int tl, int lane,
-                            int* s_hist, uint32_t (*s_mask)[kChunk / 32]) {
+// Routes token t with the calling warp: writes its top-8 (ascending expert id) with weights,
+// its local picks (ascending local expert) and their count, and adds the local picks to the
+// token's chunk histogram.
+__device__ void route_token(const RouteArgs& a, const float* s_bias, int t, int lane) {
   const float* lg = a.logits + static_cast<size_t>(t) * kEG + lane * 8;
   const float4 v0 = *reinterpret_cast<const float4*>(lg);
   const float4 v1 = *reinterpret_cast<const float4*>(lg + 4);
@@ -57,7 +57,7 @@ __device__ void route_token(const RouteArgs& a, const float* s_bias, int t, int 
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     // sigmoid as 1/(1+exp(-x)) in fp32 (reference_official.py:99); exp is evaluated in
-    // double and rounded once so it is the correctly rounded fp32 exponential.
+    // double and rounded once, i.e. the correctly rounded fp32 exponential.
     const float e = static_cast<float>(exp(-static_cast<double>(x[i])));
     s[i] = 1.0f / (1.0f + e);
     sb[i] = s[i] + s_bias[lane * 8 + i];
@@ -67,7 +67,12 @@ __device__ void route_token(const RouteArgs& a, const float* s_bias, int t, int 
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const float v = sb[i];
-    if (v > m1) { m2 = m1; m1 = v; } else if (v > m2) { m2 = v; }
+    if (v > m1) {
+      m2 = m1;
+      m1 = v;
+    } else if (v > m2) {
+      m2 = v;
+    }
   }
 #pragma unroll
   for (int d = 1; d <= 2; d <<= 1) {
@@ -87,7 +92,7 @@ __device__ void route_token(const RouteArgs& a, const float* s_bias, int t, int 
     rank += (o > gscore || (o == gscore && h < g)) ? 1 : 0;
   }
   const bool keep = rank < kTopKGroup;
-  // top-8 among kept groups: 8 rounds of a warp-wide argmax (ties -> lower expert id)
+  // top-8 among the kept groups: 8 rounds of a warp-wide argmax (ties -> lower expert id)
   uint32_t taken = 0;
 #pragma unroll 1
   for (int r = 0; r < kTopK; ++r) {
@@ -130,6 +135,7 @@ __device__ void route_token(const RouteArgs& a, const float* s_bias, int t, int 
   float* w_out = a.topk_w + static_cast<size_t>(t) * kTopK;
   int* le_out = a.tok_le + static_cast<size_t>(t) * kTopK;
   float* lw_out = a.tok_lw + static_cast<size_t>(t) * kTopK;
+  int* hist = a.chunk_hist + static_cast<size_t>(t / kChunk) * a.E;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     if ((taken >> i) & 1u) {
@@ -143,8 +149,7 @@ __device__ void route_token(const RouteArgs& a, const float* s_bias, int t, int 
         le_out[lpos] = le;
         lw_out[lpos] = w;
         ++lpos;
-        atomicAdd(&s_hist[le], 1);
-        atomicOr(&s_mask[le][tl >> 5], 1u << (tl & 31));
+        atomicAdd(hist + le, 1);
       }
     }
   }
@@ -154,12 +159,29 @@ __device__ void route_token(const RouteArgs& a, const float* s_bias, int t, int 
   if (lane == 0) a.tok_nloc[t] = nloc;
 }
 
-// Scatters the local picks of token t (chunk c, index tl in the chunk) with the calling warp:
-// row indices, row metadata, the fp8 activation row and its 56 scales.  A token with no
-// local expert gets a zero output row instead.
-__device__ void scatter_token(const RouteArgs& a, int t, int tl, int c, int lane,
+// Per-expert token bitmask of chunk c, built by the whole CTA from the tokens' pick lists.
+__device__ void build_chunk_masks(const RouteArgs& a, int c, uint32_t (*s_mask)[kChunk / 32]) {
+  for (int i = threadIdx.x; i < a.E * (kChunk / 32); i += blockDim.x) (&s_mask[0][0])[i] = 0;
+  __syncthreads();
+  const int t0 = c * kChunk;
+  const int nt = min(kChunk, a.T - t0);
+  for (int i = threadIdx.x; i < nt * kTopK; i += blockDim.x) {
+    const int tl = i / kTopK, p = i % kTopK;
+    const int t = t0 + tl;
+    if (p < __ldcg(a.tok_nloc + t)) {
+      const int le = __ldcg(a.tok_le + static_cast<size_t>(t) * kTopK + p);
+      atomicOr(&s_mask[le][tl >> 5], 1u << (tl & 31));
+    }
+  }
+  __syncthreads();
+}
+
+// Scatters the local picks of token t (index tl in its chunk) with the calling warp: row
+// indices, row metadata, the fp8 activation row and its 56 scales.  A token with no local
+// expert gets a zero output row instead.
+__device__ void scatter_token(const RouteArgs& a, int t, int tl, int lane,
                               const uint32_t (*s_mask)[kChunk / 32], const int* base) {
-  const int k = a.tok_nloc[t];
+  const int k = __ldcg(a.tok_nloc + t);
   if (k == 0) {
     uint4* dst = reinterpret_cast<uint4*>(a.out + static_cast<size_t>(t) * kH);
     for (int j = lane; j < kH * 2 / 16; j += 32) dst[j] = make_uint4(0, 0, 0, 0);
@@ -167,8 +189,8 @@ __device__ void scatter_token(const RouteArgs& a, int t, int tl, int c, int lane
   }
   int row = 0;
   if (lane < k) {
-    const int le = a.tok_le[static_cast<size_t>(t) * kTopK + lane];
-    const float w = a.tok_lw[static_cast<size_t>(t) * kTopK + lane];
+    const int le = __ldcg(a.tok_le + static_cast<size_t>(t) * kTopK + lane);
+    const float w = __ldcg(a.tok_lw + static_cast<size_t>(t) * kTopK + lane);
     int rank = 0;
     for (int wd = 0; wd < (tl >> 5); ++wd) rank += __popc(s_mask[le][wd]);
     rank += __popc(s_mask[le][tl >> 5] & ((1u << (tl & 31)) - 1u));
@@ -180,18 +202,30 @@ __device__ void scatter_token(const RouteArgs& a, int t, int tl, int c, int lane
   int rows[kTopK];
 #pragma unroll
   for (int i = 0; i < kTopK; ++i) rows[i] = __shfl_sync(0xffffffffu, row, i);
+  // the 7 KB row moves in two halves of 7 independent 16-byte loads per lane (all loads
+  // of a half issue before its stores)
   const uint4* src = reinterpret_cast<const uint4*>(a.hidden + static_cast<size_t>(t) * kH);
-  for (int j = lane; j < kH / 16; j += 32) {
-    const uint4 v = __ldg(src + j);
+  constexpr int kVec = kH / 16 / 32 / 2;   // 7 uint4 per lane per half
+  const float sc0 = a.hs_scale[static_cast<size_t>(lane) * a.T + t];
+  const float sc1 = lane + 32 < kKB1 ? a.hs_scale[static_cast<size_t>(lane + 32) * a.T + t] : 0.f;
 #pragma unroll
-    for (int i = 0; i < kTopK; ++i)
-      if (i < k) reinterpret_cast<uint4*>(a.a_perm + static_cast<size_t>(rows[i]) * kH)[j] = v;
+  for (int half = 0; half < 2; ++half) {
+    uint4 v[kVec];
+#pragma unroll
+    for (int j = 0; j < kVec; ++j) v[j] = __ldg(src + lane + 32 * (j + kVec * half));
+#pragma unroll
+    for (int i = 0; i < kTopK; ++i) {
+      if (i >= k) break;
+      uint4* dst = reinterpret_cast<uint4*>(a.a_perm + static_cast<size_t>(rows[i]) * kH);
+#pragma unroll
+      for (int j = 0; j < kVec; ++j) dst[lane + 32 * (j + kVec * half)] = v[j];
+    }
   }
-  for (int kb = lane; kb < kKB1; kb += 32) {
-    const float sc = a.hs_scale[static_cast<size_t>(kb) * a.T + t];
 #pragma unroll
-    for (int i = 0; i < kTopK; ++i)
-      if (i < k) a.sa_perm[static_cast<size_t>(kb) * a.r_pad + rows[i]] = sc;
+  for (int i = 0; i < kTopK; ++i) {
+    if (i >= k) break;
+    a.sa_perm[static_cast<size_t>(lane) * a.r_pad + rows[i]] = sc0;
+    if (lane + 32 < kKB1) a.sa_perm[static_cast<size_t>(lane + 32) * a.r_pad + rows[i]] = sc1;
   }
 }
 
@@ -214,37 +248,51 @@ __device__ int choose_split(int base_units, int sms, const int* cands, int ncand
   return best;
 }
 
-// Expert counts -> segment starts, per-chunk bases, m-tile prefix, split factors, plan.
-// Executed by one whole CTA.  `hist(c, e)` reads the chunk histogram.
-template <typename Hist>
-__device__ void scan_plan(const RouteArgs& a, Hist hist, int* s_tmp, int* s_start) {
+// Chunk counts -> expert segment starts, per-chunk bases, tile prefixes and the plan.
+// Run by one whole CTA (blockDim >= 256); zeroes the chunk counts for the next call.
+__device__ void scan_plan(const RouteArgs& a, int* s_tmp, int* s_start) {
   const int tid = threadIdx.x;
   const int E = a.E;
   int cnt = 0;
   if (tid < E)
-    for (int c = 0; c < a.nchunks; ++c) cnt += hist(c, tid);
-  // exclusive scans over experts of rows and of m-tiles (E <= 256 < blockDim)
+    for (int c0 = 0; c0 < a.nchunks; c0 += 8) {
+      int v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        v[j] = c0 + j < a.nchunks ? __ldcg(a.chunk_hist + static_cast<size_t>(c0 + j) * E + tid) : 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) cnt += v[j];
+    }
+  // inclusive scans over experts of rows and of 128-, 64- and 32-row tiles
   int* s_cnt = s_tmp;
   int* s_mt = s_tmp + 256;
+  int* s_m64 = s_tmp + 512;
+  int* s_tt = s_tmp + 768;
   if (tid < 256) {
-    s_cnt[tid] = tid < E ? cnt : 0;
-    s_mt[tid] = tid < E ? (cnt + kBlk - 1) / kBlk : 0;
+    const bool on = tid < E;
+    s_cnt[tid] = on ? cnt : 0;
+    s_mt[tid] = on ? (cnt + kBlk - 1) / kBlk : 0;
+    s_m64[tid] = on ? (cnt + 63) / 64 : 0;
+    s_tt[tid] = on ? (cnt + kTok - 1) / kTok : 0;
   }
   __syncthreads();
   for (int d = 1; d < 256; d <<= 1) {
-    int vc = 0, vm = 0;
+    int v0 = 0, v1 = 0, v2 = 0, v3 = 0;
     if (tid < 256 && tid >= d) {
-      vc = s_cnt[tid - d];
-      vm = s_mt[tid - d];
+      v0 = s_cnt[tid - d];
+      v1 = s_mt[tid - d];
+      v2 = s_m64[tid - d];
+      v3 = s_tt[tid - d];
     }
     __syncthreads();
     if (tid < 256 && tid >= d) {
-      s_cnt[tid] += vc;
-      s_mt[tid] += vm;
+      s_cnt[tid] += v0;
+      s_mt[tid] += v1;
+      s_m64[tid] += v2;
+      s_tt[tid] += v3;
     }
     __syncthreads();
   }
-  // s_cnt / s_mt now hold inclusive prefixes
   const int rows = s_cnt[255];
   const int mtiles = s_mt[255];
   __shared__ int s_split[2];
@@ -269,6 +317,8 @@ __device__ void scan_plan(const RouteArgs& a, Hist hist, int* s_tmp, int* s_star
     p.s2 = s2;
     p.kb2 = kKB2 / s2;
     p.units2 = mtiles * kNT2 * s2;
+    p.tt = s_tt[255];
+    p.m64 = s_m64[255];
     *a.plan = p;
   }
   __syncthreads();
@@ -282,10 +332,22 @@ __device__ void scan_plan(const RouteArgs& a, Hist hist, int* s_tmp, int* s_star
     a.e_mt_start[tid] = mt0;
     a.e_u1[tid] = mt0 * kNT1 * s1;
     a.e_u2[tid] = mt0 * kNT2 * s2;
+    a.e_tt[tid] = s_tt[tid] - (cnt + kTok - 1) / kTok;
+    a.e_m64[tid] = s_m64[tid] - (cnt + 63) / 64;
     int run = start;
-    for (int c = 0; c < a.nchunks; ++c) {
-      a.chunk_base[static_cast<size_t>(c) * E + tid] = run;
-      run += hist(c, tid);
+    for (int c0 = 0; c0 < a.nchunks; c0 += 8) {
+      int v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        v[j] = c0 + j < a.nchunks ? __ldcg(a.chunk_hist + static_cast<size_t>(c0 + j) * E + tid) : 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (c0 + j < a.nchunks) {
+          a.chunk_base[static_cast<size_t>(c0 + j) * E + tid] = run;
+          a.chunk_hist[static_cast<size_t>(c0 + j) * E + tid] = 0;   // self-reset for the next call
+        }
+        run += v[j];
+      }
     }
   }
   if (tid == 0) {
@@ -293,81 +355,91 @@ __device__ void scan_plan(const RouteArgs& a, Hist hist, int* s_tmp, int* s_star
     a.e_mt_start[E] = mtiles;
     a.e_u1[E] = mtiles * kNT1 * s1;
     a.e_u2[E] = mtiles * kNT2 * s2;
+    a.e_tt[E] = s_tt[255];
+    a.e_m64[E] = s_m64[255];
   }
   __syncthreads();
 }
 
-__global__ void __launch_bounds__(kRouteThreads, 1) route_kernel(RouteArgs a) {
+__global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
   __shared__ float s_bias[kEG];
-  __shared__ int s_hist[kEG];
   __shared__ uint32_t s_mask[kEG][kChunk / 32];
-  __shared__ int s_tmp[512];
+  __shared__ int s_tmp[1024];
   __shared__ int s_start[kEG];
   __shared__ int s_last;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int c = blockIdx.x;
-  for (int i = tid; i < kEG; i += blockDim.x) {
-    s_bias[i] = bf16_bits_to_float(a.bias[i]);
-    s_hist[i] = 0;
-  }
-  for (int i = tid; i < kEG * (kChunk / 32); i += blockDim.x) (&s_mask[0][0])[i] = 0;
+  for (int i = tid; i < kEG; i += blockDim.x) s_bias[i] = bf16_bits_to_float(a.bias[i]);
   __syncthreads();
-  const int t0 = c * kChunk;
-  const int nt = min(kChunk, a.T - t0);
-  for (int tl = warp; tl < nt; tl += kRouteThreads / 32)
-    route_token(a, s_bias, t0 + tl, tl, lane, s_hist, s_mask);
-  __syncthreads();
-  if (a.nchunks == 1) {
-    scan_plan(a, [&](int, int e) { return s_hist[e]; }, s_tmp, s_start);
-    for (int tl = warp; tl < nt; tl += kRouteThreads / 32)
-      scatter_token(a, t0 + tl, tl, 0, lane, s_mask, s_start);
-    return;
-  }
-  for (int e = tid; e < a.E; e += blockDim.x) a.chunk_hist[static_cast<size_t>(c) * a.E + e] = s_hist[e];
+  const int t = blockIdx.x * kRouteWarps + warp;
+  if (t < a.T) route_token(a, s_bias, t, lane);
   __threadfence();
   __syncthreads();
   if (tid == 0) {
     const int prev = atomicAdd(a.route_done, 1);
-    s_last = (prev == a.nchunks - 1);
+    s_last = (prev == static_cast<int>(gridDim.x) - 1);
   }
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  const int* hist = a.chunk_hist;
-  const int E = a.E;
-  scan_plan(a, [&](int cc, int e) { return __ldcg(hist + static_cast<size_t>(cc) * E + e); }, s_tmp,
-            s_start);
+  scan_plan(a, s_tmp, s_start);
   if (tid == 0) *a.route_done = 0;   // self-reset for the next call
+  if (a.nchunks == 1) {
+    build_chunk_masks(a, 0, s_mask);
+    for (int tl = warp; tl < a.T; tl += kRouteWarps) scatter_token(a, tl, tl, lane, s_mask, s_start);
+  }
 }
 
-__global__ void __launch_bounds__(kRouteThreads, 1) scatter_kernel(RouteArgs a) {
+__global__ void __launch_bounds__(kRouteThreads) scatter_kernel(RouteArgs a) {
   __shared__ uint32_t s_mask[kEG][kChunk / 32];
   __shared__ int s_base[kEG];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  pdl_launch_dependents();
+  const int t0 = blockIdx.x * kRouteWarps;   // this CTA's tokens: t0 .. t0+7 (one chunk)
+  const int c = t0 / kChunk;
+  for (int e = threadIdx.x; e < a.E; e += blockDim.x) s_base[e] = a.chunk_base[static_cast<size_t>(c) * a.E + e];
+  build_chunk_masks(a, c, s_mask);
+  const int t = t0 + warp;
+  if (t < a.T) scatter_token(a, t, t - c * kChunk, lane, s_mask, s_base);
+}
+
+// T <= kRouteSmallT: one CTA of 32 warps routes every token, scans and scatters in a single
+// launch (the decode regime, where the routing latency is on the layer's critical path).
+constexpr int kRouteSmallT = 256;
+constexpr int kRouteSmallThreads = 1024;
+
+__global__ void __launch_bounds__(kRouteSmallThreads, 1) route_small_kernel(RouteArgs a) {
+  __shared__ float s_bias[kEG];
+  __shared__ uint32_t s_mask[kEG][kChunk / 32];
+  __shared__ int s_tmp[1024];
+  __shared__ int s_start[kEG];
+  __shared__ int s_base[kEG];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int c = blockIdx.x;
-  for (int i = tid; i < kEG * (kChunk / 32); i += blockDim.x) (&s_mask[0][0])[i] = 0;
-  for (int e = tid; e < a.E; e += blockDim.x) s_base[e] = a.chunk_base[static_cast<size_t>(c) * a.E + e];
+  pdl_launch_dependents();   // the GEMM that follows may run its prologue meanwhile
+  for (int i = tid; i < kEG; i += blockDim.x) s_bias[i] = bf16_bits_to_float(a.bias[i]);
   __syncthreads();
-  const int t0 = c * kChunk;
-  const int nt = min(kChunk, a.T - t0);
-  for (int tl = warp; tl < nt; tl += kRouteThreads / 32) {
-    const int t = t0 + tl;
-    const int k = a.tok_nloc[t];
-    if (lane < k) {
-      const int le = a.tok_le[static_cast<size_t>(t) * kTopK + lane];
-      atomicOr(&s_mask[le][tl >> 5], 1u << (tl & 31));
-    }
+  for (int t = warp; t < a.T; t += kRouteSmallThreads / 32) route_token(a, s_bias, t, lane);
+  __syncthreads();
+  scan_plan(a, s_tmp, s_start);
+  for (int c = 0; c < a.nchunks; ++c) {
+    for (int e = tid; e < a.E; e += blockDim.x) s_base[e] = c == 0 ? s_start[e] : __ldcg(a.chunk_base + static_cast<size_t>(c) * a.E + e);
+    build_chunk_masks(a, c, s_mask);
+    const int t0 = c * kChunk, nt = min(kChunk, a.T - t0);
+    for (int tl = warp; tl < nt; tl += kRouteSmallThreads / 32) scatter_token(a, t0 + tl, tl, lane, s_mask, s_base);
+    __syncthreads();
   }
-  __syncthreads();
-  for (int tl = warp; tl < nt; tl += kRouteThreads / 32)
-    scatter_token(a, t0 + tl, tl, c, lane, s_mask, s_base);
 }
 
 cudaError_t route_launch(const RouteArgs& a, cudaStream_t st, int* launches) {
-  route_kernel<<<a.nchunks, kRouteThreads, 0, st>>>(a);
+  if (a.T <= kRouteSmallT) {
+    route_small_kernel<<<1, kRouteSmallThreads, 0, st>>>(a);
+    ++*launches;
+    return cudaGetLastError();
+  }
+  const int grid = (a.T + kRouteWarps - 1) / kRouteWarps;
+  route_kernel<<<grid, kRouteThreads, 0, st>>>(a);
   ++*launches;
   if (a.nchunks > 1) {
-    scatter_kernel<<<a.nchunks, kRouteThreads, 0, st>>>(a);
+    scatter_kernel<<<grid, kRouteThreads, 0, st>>>(a);
     ++*launches;
   }
   return cudaGetLastError();

@@ -1,0 +1,611 @@
+// Weight-streaming grouped GEMMs for small and mid T (decode regime), tcgen05 on sm_100a.
+//
+// Orientation is weight-major ("swap AB"): a tile is 128 weight rows (MMA M) times a
+// 32-token tile of one expert (MMA N = 32), so an expert with a handful of routed tokens
+// costs one N=32 MMA per 128x128 weight block and every weight byte is read from HBM once.
+//
+//   MODE 1 (GEMM1): tile = (expert, 32-token tile, pair tile nt of 128 X1 rows [128nt, +128)
+//     and 128 X2 rows [2048+128nt, +128)); K = 56 blocks of 128.
+//       D1 = W13[X1 rows] . A^T,  D2 = W13[X2 rows] . A^T   (fp8 x fp8 -> fp32 TMEM)
+//       acc_i[r][c] += D_i[r][c] * s13[e, block_i, kb] * sa[token c, kb]   (exact fp32 scales)
+//     epilogue: C = silu(X2) * X1 per (feature r, token c); per-token amax over the tile's
+//     128 features; C stored as the hi/lo e4m3 pair C ~= s*(hi + lo/16), s = amax/448.
+//   MODE 2 (GEMM2): tile = (expert, 32-token tile, 128 output features nt); K = 16 blocks.
+//       D_hi = W2 . C_hi^T,  D_lo = W2 . C_lo^T
+//       acc[r][c] += (D_hi + D_lo/16)[r][c] * s2[e, nt, kb] * sc[token c, kb]
+//     epilogue: out[t, f] = bf16(w * O) for a token with one local expert; otherwise the
+//     token's rows are summed in ascending expert order by the last contributing tile
+//     (per-(token, 128-feature) arrival counter) -- deterministic.
+//
+// Work is split stream-K over the persistent CTAs (sched.cuh), so all SMs stream weights
+// even when routing activates a few experts.  CTA = 6 warps: warp 0 TMA producer, warp 1
+// TMEM owner + single-thread MMA issuer, warps 2..5 promotion/epilogue (one per TMEM lane
+// quarter; thread = weight row).  5 (MODE 1) / 8 (MODE 2) smem stages, 8 TMEM accumulator
+// buffers of 64 columns, so the MMA runs up to 8 K-blocks ahead of the promotion.  No TMA
+// multicast (the kernels also run in the multi-GPU expert-parallel configuration).
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "launch_args.cuh"
+#include "moe_internal.cuh"
+#include "ptx.cuh"
+#include "sched.cuh"
+
+namespace moe {
+
+// Per-CTA role counters of a traced build: [0] start ns, [1] end ns, [2] producer cycles
+// waiting for a free stage, [3] K-blocks issued, [4] MMA cycles waiting for data, [5] MMA
+// cycles waiting for a free TMEM buffer, [6] epilogue cycles waiting for an accumulator,
+// [7] epilogue promotion cycles, [8] tile-epilogue cycles, [9] stream-K fixup cycles,
+// [10] scale-staging cycles, [11] first data arrival ns.
+#ifdef MOE_TRACE
+#define MOE_TCLK() clock64()
+#define MOE_TADD(var, t0) (var) += clock64() - (t0)
+#else
+#define MOE_TCLK() 0ll
+#define MOE_TADD(var, t0) (void)0
+#endif
+
+template <int MODE>
+struct SCfg;
+template <>
+struct SCfg<1> {
+  static constexpr int KB = kKB1;
+  static constexpr int NT = kNT1;
+  static constexpr int STAGES = 5;
+  static constexpr int STAGE_BYTES = 2 * 16384 + kTok * 128;   // W X1 | W X2 | tokens
+};
+template <>
+struct SCfg<2> {
+  static constexpr int KB = kKB2;
+  static constexpr int NT = kNT2;
+  static constexpr int STAGES = 8;
+  static constexpr int STAGE_BYTES = 16384 + 2 * kTok * 128;   // W2 | C hi | C lo
+};
+
+constexpr int kSBufs = 8;          // TMEM accumulator buffers (64 columns each)
+constexpr int kSThreads = 192;
+constexpr int kSEpiThreads = 128;
+
+template <int MODE>
+struct StreamSmem {
+  uint8_t stage[SCfg<MODE>::STAGES][SCfg<MODE>::STAGE_BYTES];
+  uint8_t ostage[MODE == 1 ? 2 : 1][MODE == 1 ? kTok : 1][128];   // MODE 1: hi/lo bytes, [token][feature]
+  float ssa[SCfg<MODE>::KB][kTok];   // this segment's token scales, [K-block][token column]
+  float ssw[2][SCfg<MODE>::KB];      // this segment's weight scales (MODE 1: X1, X2 blocks)
+  uint64_t full[SCfg<MODE>::STAGES];
+  uint64_t empty[SCfg<MODE>::STAGES];
+  uint64_t tfull[kSBufs];
+  uint64_t tempty[kSBufs];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+  int flag;
+  int colflag[kTok];
+  int col_t[kTok];
+  int col_k[kTok];
+  float col_w[kTok];
+  float colmax[4][kTok];
+  float amax[kTok];
+  int e_cnt[kEG + 1];
+  int e_start[kEG + 1];
+  int e_tt[kEG + 1];
+};
+
+template <int MODE>
+constexpr size_t stream_smem_bytes() {
+  return sizeof(StreamSmem<MODE>) + 1024;
+}
+
+struct STile {
+  int e, nt, row0, nr;
+};
+
+template <int MODE>
+__device__ __forceinline__ STile s_decode(const StreamSmem<MODE>& sm, int E, int tile) {
+  constexpr int NT = SCfg<MODE>::NT;
+  int lo = 0, hi = E - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (sm.e_tt[mid] * NT <= tile) lo = mid; else hi = mid - 1;
+  }
+  const int v = tile - sm.e_tt[lo] * NT;
+  const int jt = sm.e_tt[lo + 1] - sm.e_tt[lo];
+  STile s;
+  s.e = lo;
+  s.nt = v / jt;
+  const int j = v - s.nt * jt;
+  s.row0 = sm.e_start[lo] + kTok * j;
+  s.nr = min(kTok, sm.e_cnt[lo] - kTok * j);
+  return s;
+}
+
+__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
+
+__device__ __forceinline__ uint16_t bf16_bits(float v) {
+  __nv_bfloat16 b = __float2bfloat16_rn(v);
+  return *reinterpret_cast<uint16_t*>(&b);
+}
+
+template <int MODE>
+__device__ void s_producer(StreamSmem<MODE>& sm, const CUtensorMap* tmW, const CUtensorMap* tmT,
+                           const CUtensorMap* tmT2, const TileArgs& g, const Sched& sk) {
+  constexpr int ST = SCfg<MODE>::STAGES;
+  uint32_t stage = 0, phase = 0, issued = 0, lastpar = 0;
+  long long tw = 0, nkb = 0;
+  // MODE 2: the first ST stages get their weight tiles before the dependency on GEMM1 is
+  // resolved; their token tiles follow the wait.
+  int pend_n = 0;
+  int pend_row0[ST];
+  int pend_kb[ST];
+  bool waited = MODE == 1;
+  SegIter it(sk, blockIdx.x);
+  int tile, k0, k1;
+  while (it.next(tile, k0, k1)) {
+    const STile s = s_decode<MODE>(sm, g.E, tile);
+    for (int kb = k0; kb < k1; ++kb) {
+      const long long t0 = MOE_TCLK();
+      if (!mbar_wait(&sm.empty[stage], phase ^ 1u, &sm.abort, g.status, kStWaitProducer)) goto drain;
+      MOE_TADD(tw, t0);
+      ++nkb;
+      mbar_arrive_expect_tx(&sm.full[stage], SCfg<MODE>::STAGE_BYTES);
+      uint8_t* st = sm.stage[stage];
+      if (MODE == 1) {
+        tma_load_2d(st, tmW, &sm.full[stage], kb * kBlk, s.e * kN1 + s.nt * kBlk);
+        tma_load_2d(st + 16384, tmW, &sm.full[stage], kb * kBlk, s.e * kN1 + kI + s.nt * kBlk);
+        tma_load_2d(st + 32768, tmT, &sm.full[stage], kb * kBlk, s.row0);
+      } else {
+        tma_load_2d(st, tmW, &sm.full[stage], kb * kBlk, s.e * kH + s.nt * kBlk);
+        if (!waited) {
+          pend_row0[pend_n] = s.row0;
+          pend_kb[pend_n] = kb;
+          ++pend_n;
+        } else {
+          tma_load_2d(st + 16384, tmT, &sm.full[stage], kb * kBlk, s.row0);
+          tma_load_2d(st + 16384 + kTok * 128, tmT2, &sm.full[stage], kb * kBlk, s.row0);
+        }
+      }
+      issued |= 1u << stage;
+      lastpar = (lastpar & ~(1u << stage)) | (phase << stage);
+      if (++stage == ST) {
+        stage = 0;
+        phase ^= 1u;
+      }
+      if (MODE == 2 && !waited && pend_n == ST) {
+        pdl_wait();
+        waited = true;
+        for (int i = 0; i < pend_n; ++i) {
+          uint8_t* sp = sm.stage[i];
+          tma_load_2d(sp + 16384, tmT, &sm.full[i], pend_kb[i] * kBlk, pend_row0[i]);
+          tma_load_2d(sp + 16384 + kTok * 128, tmT2, &sm.full[i], pend_kb[i] * kBlk, pend_row0[i]);
+        }
+        pend_n = 0;
+      }
+    }
+  }
+  if (MODE == 2 && !waited) {   // fewer K-blocks than stages
+    pdl_wait();
+    for (int i = 0; i < pend_n; ++i) {
+      uint8_t* sp = sm.stage[i];
+      tma_load_2d(sp + 16384, tmT, &sm.full[i], pend_kb[i] * kBlk, pend_row0[i]);
+      tma_load_2d(sp + 16384 + kTok * 128, tmT2, &sm.full[i], pend_kb[i] * kBlk, pend_row0[i]);
+    }
+  }
+drain:
+  for (int s = 0; s < ST; ++s)
+    if ((issued >> s) & 1u) {
+      int no_abort = 0;
+      mbar_wait(&sm.full[s], (lastpar >> s) & 1u, &no_abort, g.status, kStWaitDrain);
+    }
+#ifdef MOE_TRACE
+  g.trace[blockIdx.x * kTraceSlots + 2] = tw;
+  g.trace[blockIdx.x * kTraceSlots + 3] = nkb;
+#endif
+}
+
+template <int MODE>
+__device__ void s_mma(StreamSmem<MODE>& sm, uint32_t tmem, const TileArgs& g, const Sched& sk) {
+  constexpr int ST = SCfg<MODE>::STAGES;
+  constexpr uint32_t idesc = idesc_e4m3_f32(128, kTok);
+  uint32_t stage = 0, phase = 0, tk = 0, buf = 0;
+  long long tw_t = 0, tw_f = 0, t_first = 0;
+  SegIter it(sk, blockIdx.x);
+  int tile, k0, k1;
+  while (it.next(tile, k0, k1)) {
+    for (int kb = k0; kb < k1; ++kb) {
+      long long t0 = MOE_TCLK();
+      if (!mbar_wait(&sm.tempty[buf], ((tk >> buf) & 1u) ^ 1u, &sm.abort, g.status, kStWaitMmaTmem))
+        goto done;
+      MOE_TADD(tw_t, t0);
+      t0 = MOE_TCLK();
+      if (!mbar_wait(&sm.full[stage], phase, &sm.abort, g.status, kStWaitMma)) goto done;
+      MOE_TADD(tw_f, t0);
+#ifdef MOE_TRACE
+      if (t_first == 0) t_first = static_cast<long long>(globaltimer_ns());
+#endif
+      tc_fence_after();
+      {
+        const uint32_t st = smem_u32(sm.stage[stage]);
+        const uint32_t d = tmem + buf * 64u;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          if (MODE == 1) {
+            const uint64_t bt = sdesc_k128_sw128(st + 32768 + 32 * k);
+            mma_f8f6f4(d, sdesc_k128_sw128(st + 32 * k), bt, idesc, k > 0);
+            mma_f8f6f4(d + 32u, sdesc_k128_sw128(st + 16384 + 32 * k), bt, idesc, k > 0);
+          } else {
+            const uint64_t aw = sdesc_k128_sw128(st + 32 * k);
+            mma_f8f6f4(d, aw, sdesc_k128_sw128(st + 16384 + 32 * k), idesc, k > 0);
+            mma_f8f6f4(d + 32u, aw, sdesc_k128_sw128(st + 16384 + kTok * 128 + 32 * k), idesc, k > 0);
+          }
+        }
+      }
+      mma_commit(&sm.empty[stage]);
+      mma_commit(&sm.tfull[buf]);
+      tk ^= 1u << buf;
+      buf = (buf + 1) & (kSBufs - 1);
+      if (++stage == ST) {
+        stage = 0;
+        phase ^= 1u;
+      }
+    }
+  }
+done:
+  mma_commit(&sm.drain);
+  int no_abort = 0;
+  mbar_wait(&sm.drain, 0, &no_abort, g.status, kStWaitDrain);
+#ifdef MOE_TRACE
+  g.trace[blockIdx.x * kTraceSlots + 4] = tw_f;
+  g.trace[blockIdx.x * kTraceSlots + 5] = tw_t;
+  g.trace[blockIdx.x * kTraceSlots + 11] = t_first;
+#endif
+}
+
+// MODE 1 tile epilogue: SwiGLU, per-token amax over the 128 features, hi/lo e4m3 encoding.
+__device__ void s_epi1(StreamSmem<1>& sm, const TileArgs& g, const STile& s, float* x1, const float* x2,
+                       int q, int lane) {
+  const int r = q * 32 + lane;
+  float m[kTok];
+#pragma unroll
+  for (int c = 0; c < kTok; ++c) {
+    const float v = silu_f(x2[c]) * x1[c];
+    x1[c] = v;
+    m[c] = fabsf(v);
+  }
+  warp_colmax32(m, lane);
+  sm.colmax[q][lane] = m[0];
+  named_bar_sync(1, kSEpiThreads);
+  if (q == 0) {
+    const float a = fmaxf(fmaxf(sm.colmax[0][lane], sm.colmax[1][lane]), fmaxf(sm.colmax[2][lane], sm.colmax[3][lane]));
+    sm.amax[lane] = a;
+    if (lane < s.nr)
+      g.c_scale[static_cast<size_t>(s.nt) * g.r_pad + s.row0 + lane] = a > 0.f ? a / 448.0f : 1.0f;
+  }
+  named_bar_sync(1, kSEpiThreads);
+#pragma unroll
+  for (int c = 0; c < kTok; c += 2) {
+    const float a0 = sm.amax[c], a1 = sm.amax[c + 1];
+    const float y0 = x1[c] * (a0 > 0.f ? 448.0f / a0 : 0.f);
+    const float y1 = x1[c + 1] * (a1 > 0.f ? 448.0f / a1 : 0.f);
+    const uint32_t h = cvt_e4m3x2(y0, y1);
+    const float2 b = e4m3x2_to_f2(static_cast<uint16_t>(h));
+    const uint32_t l = cvt_e4m3x2((y0 - b.x) * 16.f, (y1 - b.y) * 16.f);
+    sm.ostage[0][c][r] = static_cast<uint8_t>(h & 0xFF);
+    sm.ostage[0][c + 1][r] = static_cast<uint8_t>(h >> 8);
+    sm.ostage[1][c][r] = static_cast<uint8_t>(l & 0xFF);
+    sm.ostage[1][c + 1][r] = static_cast<uint8_t>(l >> 8);
+  }
+  named_bar_sync(1, kSEpiThreads);
+  const int tid = q * 32 + lane;
+  for (int i = tid; i < 2 * kTok * 8; i += kSEpiThreads) {
+    const int h = i / (kTok * 8), c = (i / 8) % kTok, ch = i % 8;
+    if (c < s.nr) {
+      uint8_t* dst = (h == 0 ? g.c_hi : g.c_lo) + static_cast<size_t>(s.row0 + c) * kI + s.nt * kBlk + ch * 16;
+      *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(&sm.ostage[h][c][ch * 16]);
+    }
+  }
+  named_bar_sync(1, kSEpiThreads);
+}
+
+// MODE 2 tile epilogue: routing-weighted, expert-ordered combine into the bf16 output.
+__device__ void s_epi2(StreamSmem<2>& sm, const TileArgs& g, const STile& s, const float* acc, int q,
+                       int lane) {
+  const int r = q * 32 + lane;
+  const int f = s.nt * kBlk + r;
+  if (q == 0) {   // lane c loads token column c's metadata (one round of loads for the tile)
+    int t = 0, kt = 0;
+    float w = 0.f;
+    if (lane < s.nr) {
+      t = __ldg(g.row_token + s.row0 + lane);
+      w = __ldg(g.row_weight + s.row0 + lane);
+      kt = __ldg(g.tok_nloc + t);
+    }
+    sm.col_t[lane] = t;
+    sm.col_k[lane] = kt;
+    sm.col_w[lane] = w;
+  }
+  named_bar_sync(1, kSEpiThreads);
+#pragma unroll
+  for (int c = 0; c < kTok; ++c) {
+    if (c >= s.nr) break;
+    const int t = sm.col_t[c];
+    if (sm.col_k[c] == 1)
+      g.out[static_cast<size_t>(t) * kH + f] = bf16_bits(__fmul_rn(acc[c], sm.col_w[c]));
+    else
+      g.part2[static_cast<size_t>(s.row0 + c) * kH + f] = acc[c];
+  }
+  named_bar_sync(1, kSEpiThreads);
+  if (q == 0) {
+    int fl = 0;
+    const int kt = sm.col_k[lane];
+    if (lane < s.nr && kt > 1) {
+      int* ctr = g.cnt2 + static_cast<size_t>(sm.col_t[lane]) * kNT2 + s.nt;
+      const int prev = atomic_add_acq_rel_gpu(ctr, 1);
+      if (prev == kt - 1) {
+        *ctr = 0;   // last contributor: reset for the next call
+        fl = 1;
+      }
+    }
+    sm.colflag[lane] = fl;
+  }
+  named_bar_sync(1, kSEpiThreads);
+  for (int c = 0; c < s.nr; ++c) {
+    if (!sm.colflag[c]) continue;
+    const int t = sm.col_t[c];
+    const int kt = sm.col_k[c];
+    int ra[kTopK];
+    float wa[kTopK];
+#pragma unroll
+    for (int a = 0; a < kTopK; ++a) {
+      ra[a] = a < kt ? __ldg(g.tok_rows + static_cast<size_t>(t) * kTopK + a) : 0;
+    }
+#pragma unroll
+    for (int a = 0; a < kTopK; ++a) wa[a] = a < kt ? __ldg(g.row_weight + ra[a]) : 0.f;
+    float o[kTopK];
+#pragma unroll
+    for (int a = 0; a < kTopK; ++a) o[a] = a < kt ? __ldcg(g.part2 + static_cast<size_t>(ra[a]) * kH + f) : 0.f;
+    float sum = 0.f;
+#pragma unroll
+    for (int a = 0; a < kTopK; ++a)
+      if (a < kt) sum = __fadd_rn(sum, __fmul_rn(o[a], wa[a]));
+    g.out[static_cast<size_t>(t) * kH + f] = bf16_bits(sum);
+  }
+  named_bar_sync(1, kSEpiThreads);
+}
+
+template <int MODE>
+__device__ void s_epilogue(StreamSmem<MODE>& sm, uint32_t tmem, const TileArgs& g, const Sched& sk,
+                           int warp, int lane) {
+  const int q = warp & 3;
+  const int r = q * 32 + lane;
+  const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
+  uint32_t tk = 0, buf = 0;
+  bool dead = false;
+  long long tw = 0, tp = 0, te = 0, tf = 0, ts = 0;
+  if (MODE == 2) pdl_wait();   // the C scales and the combine inputs come from GEMM1
+  SegIter it(sk, blockIdx.x);
+  int tile, k0, k1;
+  while (it.next(tile, k0, k1)) {
+    const STile s = s_decode<MODE>(sm, g.E, tile);
+    long long t0 = MOE_TCLK();
+    // lane c prefetches the scale of token column c (clamped to a routed row of this tile)
+    const size_t srow = static_cast<size_t>(s.row0 + min(lane, s.nr - 1));
+    float acc1[kTok], acc2[kTok];
+#pragma unroll
+    for (int c = 0; c < kTok; ++c) {
+      acc1[c] = 0.f;
+      acc2[c] = 0.f;
+    }
+    const float* swp1;
+    const float* swp2;
+    if (MODE == 1) {
+      swp1 = g.sw + (static_cast<size_t>(s.e) * 32 + s.nt) * kKB1;
+      swp2 = g.sw + (static_cast<size_t>(s.e) * 32 + kNT1 + s.nt) * kKB1;
+    } else {
+      swp1 = g.sw + (static_cast<size_t>(s.e) * kNT2 + s.nt) * kKB2;
+      swp2 = swp1;
+    }
+    // stage the segment's scales in shared memory: one round of independent loads per
+    // segment instead of an L2 round trip on every K-block's critical path
+    for (int i = q; i < k1 - k0; i += 4) sm.ssa[i][lane] = __ldg(g.sa + static_cast<size_t>(k0 + i) * g.r_pad + srow);
+    if (q == 0)
+      for (int i = lane; i < k1 - k0; i += 32) {
+        sm.ssw[0][i] = __ldg(swp1 + k0 + i);
+        sm.ssw[1][i] = __ldg(swp2 + k0 + i);
+      }
+    named_bar_sync(1, kSEpiThreads);
+    MOE_TADD(ts, t0);
+    for (int kb = k0; kb < k1; ++kb) {
+      const int ki = kb - k0;
+      const float w1 = sm.ssw[0][ki], w2 = sm.ssw[1][ki];
+      t0 = MOE_TCLK();
+      if (!dead && !mbar_wait(&sm.tfull[buf], (tk >> buf) & 1u, &sm.abort, g.status, kStWaitEpilogue))
+        dead = true;
+      MOE_TADD(tw, t0);
+      t0 = MOE_TCLK();
+      if (!dead) {
+        tc_fence_after();
+        float d1[kTok], d2[kTok];
+        tmem_ld32x2_wait(lane_base + buf * 64u, lane_base + buf * 64u + 32u, d1, d2);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.tempty[buf]);
+        const float4* sv = reinterpret_cast<const float4*>(sm.ssa[ki]);
+#pragma unroll
+        for (int c = 0; c < kTok; ++c) {
+          const float4 s4 = sv[c / 4];
+          const float sc = (c & 3) == 0 ? s4.x : (c & 3) == 1 ? s4.y : (c & 3) == 2 ? s4.z : s4.w;
+          if (MODE == 1) {
+            acc1[c] = fmaf(d1[c], sc * w1, acc1[c]);
+            acc2[c] = fmaf(d2[c], sc * w2, acc2[c]);
+          } else {
+            acc1[c] = fmaf(fmaf(d2[c], 0.0625f, d1[c]), sc * w1, acc1[c]);
+          }
+        }
+      }
+      MOE_TADD(tp, t0);
+      tk ^= 1u << buf;
+      buf = (buf + 1) & (kSBufs - 1);
+    }
+    t0 = MOE_TCLK();
+    const bool full = (k0 == 0 && k1 == SCfg<MODE>::KB);
+    if (!full) {
+      // stream-K fixup: publish this CTA's partial, the last contributor sums them in CTA order
+      constexpr int NH = MODE == 1 ? 2 : 1;
+      const int slot = sk.slot(blockIdx.x, tile);
+      float* p = g.part + static_cast<size_t>(slot) * NH * kTok * 128;
+#pragma unroll
+      for (int c = 0; c < kTok; ++c) {
+        p[c * 128 + r] = acc1[c];
+        if (MODE == 1) p[(kTok + c) * 128 + r] = acc2[c];
+      }
+      named_bar_sync(1, kSEpiThreads);
+      if (q == 0 && lane == 0) {
+        const int expect = sk.last_cta(tile) - sk.first_cta(tile) + 1;
+        const int prev = atomic_add_acq_rel_gpu(g.tile_cnt + tile, 1);
+        const int last = prev == expect - 1;
+        if (last) g.tile_cnt[tile] = 0;
+        sm.flag = last;
+      }
+      named_bar_sync(1, kSEpiThreads);
+      const int last = sm.flag;
+      named_bar_sync(1, kSEpiThreads);
+      if (!last) {
+        MOE_TADD(tf, t0);
+        continue;
+      }
+#pragma unroll
+      for (int c = 0; c < kTok; ++c) {
+        acc1[c] = 0.f;
+        acc2[c] = 0.f;
+      }
+      for (int cta = sk.first_cta(tile); cta <= sk.last_cta(tile); ++cta) {
+        const float* pp = g.part + static_cast<size_t>(sk.slot(cta, tile)) * NH * kTok * 128;
+#pragma unroll
+        for (int c = 0; c < kTok; ++c) {
+          acc1[c] += __ldcg(pp + c * 128 + r);
+          if (MODE == 1) acc2[c] += __ldcg(pp + (kTok + c) * 128 + r);
+        }
+      }
+    }
+    MOE_TADD(tf, t0);
+    t0 = MOE_TCLK();
+    // (after an abort the epilogue still runs, on garbage, so every warp meets every barrier)
+    if (MODE == 1)
+      s_epi1(reinterpret_cast<StreamSmem<1>&>(sm), g, s, acc1, acc2, q, lane);
+    else
+      s_epi2(reinterpret_cast<StreamSmem<2>&>(sm), g, s, acc1, q, lane);
+    MOE_TADD(te, t0);
+  }
+#ifdef MOE_TRACE
+  if (warp == 2 && lane == 0) {
+    unsigned long long* tr = g.trace + blockIdx.x * kTraceSlots;
+    tr[6] = tw;
+    tr[7] = tp;
+    tr[8] = te;
+    tr[9] = tf;
+    tr[10] = ts;
+    tr[1] = globaltimer_ns();
+  }
+#endif
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kSThreads, 1)
+    stream_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmT,
+                  const __grid_constant__ CUtensorMap tmT2, TileArgs g) {
+  extern __shared__ uint8_t smem_raw[];
+  StreamSmem<MODE>& sm =
+      *reinterpret_cast<StreamSmem<MODE>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // GEMM1 depends on the routing kernel for everything; GEMM2 reads only the plan (routing,
+  // complete once GEMM1 started) before its own wait, so it can prefetch weights while
+  // GEMM1 finishes.
+  if (MODE == 1) {
+    pdl_wait();
+    pdl_launch_dependents();
+  }
+  const Plan plan = *g.plan;
+  Sched sk;
+  sk.init(plan.tt * SCfg<MODE>::NT, gridDim.x, SCfg<MODE>::KB);
+  if (plan.tt == 0 || !sk.has_work(blockIdx.x)) return;   // no work for this CTA
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i <= g.E; i += blockDim.x) {
+    sm.e_cnt[i] = i < g.E ? g.e_count[i] : 0;
+    sm.e_start[i] = g.e_start[i];
+    sm.e_tt[i] = g.e_tiles[i];
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < SCfg<MODE>::STAGES; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], 1);
+    }
+    for (int b = 0; b < kSBufs; ++b) {
+      mbar_init(&sm.tfull[b], 1);
+      mbar_init(&sm.tempty[b], 4);
+    }
+    mbar_init(&sm.drain, 1);
+    sm.abort = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmW);
+    tma_prefetch_desc(&tmT);
+    tma_prefetch_desc(&tmT2);
+  }
+  if (warp == 1) {
+    tmem_alloc(&sm.tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+#ifdef MOE_TRACE
+  if (threadIdx.x == 0) g.trace[blockIdx.x * kTraceSlots + 0] = globaltimer_ns();
+#endif
+  const uint32_t tmem = sm.tmem_base;
+  if (warp == 0) {
+    if (lane == 0) s_producer<MODE>(sm, &tmW, &tmT, &tmT2, g, sk);
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) s_mma<MODE>(sm, tmem, g, sk);
+    __syncwarp();
+  } else {
+    s_epilogue<MODE>(sm, tmem, g, sk, warp, lane);
+    __syncwarp();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+cudaError_t stream_prepare() {
+  cudaError_t e = cudaFuncSetAttribute(stream_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(stream_smem_bytes<1>()));
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(stream_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(stream_smem_bytes<2>()));
+}
+
+// Launched as programmatic dependents of the preceding kernel in the stream (PDL).
+cudaError_t stream_launch(int mode, int grid, cudaStream_t st, const CUtensorMap& w, const CUtensorMap& t,
+                          const CUtensorMap& t2, const TileArgs& g) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kSThreads);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (mode == 1) {
+    cfg.dynamicSmemBytes = stream_smem_bytes<1>();
+    return cudaLaunchKernelEx(&cfg, stream_kernel<1>, w, t, t2, g);
+  }
+  cfg.dynamicSmemBytes = stream_smem_bytes<2>();
+  return cudaLaunchKernelEx(&cfg, stream_kernel<2>, w, t, t2, g);
+}
+
+}  // namespace moe

@@ -1,0 +1,624 @@
+// Token-major grouped GEMMs for large T (prefill / expert-parallel batches), tcgen05 on
+// sm_100a.  A tile is a block of routed token rows of one expert (MMA M = 128 rows) times
+// 256 weight rows (MMA N = 256), so the tensor core runs at its full-width shape and every
+// token row's fp32 scale is a per-thread scalar in the promotion.
+//
+//   MODE 1 (GEMM1): tile = (expert, 128-row token tile, pair tile nt: 128 X1 rows [128nt, +128)
+//     and 128 X2 rows [2048+128nt, +128)); K = 56 blocks.  D = A . [W_X1 | W_X2]^T.
+//       acc[r][c] += D[r][c] * sa[r, kb] * s13[e, block(c), kb]
+//     epilogue: C = silu(X2) * X1, stored as the hi/lo e4m3 pair C ~= s*(hi + lo/16) with one
+//     scale per (row, 128 columns), s = amax/448.
+//   MODE 2 (GEMM2): tile = (expert, 64-token tile, 256 output features nt); K = 16 blocks.
+//     The A tile holds each token twice, as its hi row and its lo row, interleaved in groups
+//     of 16 so that a token's two rows sit in one TMEM lane quarter: smem/TMEM row
+//     32q + i (i < 16) is hi of token 16q + i, row 32q + 16 + i is lo of the same token.
+//       acc[r][c] += D[r][c] * sc[token(r), kb] * s2[e, nt, kb] * (lo ? 1/16 : 1)
+//     epilogue: one shuffle adds a token's lo half to its hi half; then the routing-weighted,
+//     expert-ordered combine into the bf16 output (direct for a token with one local expert,
+//     else through the per-(token, 256-feature) arrival counter).
+//
+// CTA = 10 warps: warp 0 TMA producer, warp 1 TMEM owner + single-thread MMA issuer,
+// warps 2..9 promotion/epilogue: two warps per TMEM lane quarter, one per column half.
+// 4 smem stages of 48 KB, 2 TMEM accumulator buffers of 256 columns.  Work: data-parallel
+// whole tiles, then a stream-K tail (sched.cuh).  No TMA multicast (the kernels also run in the
+// multi-GPU expert-parallel configuration).
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "launch_args.cuh"
+#include "moe_internal.cuh"
+#include "ptx.cuh"
+#include "sched.cuh"
+
+namespace moe {
+
+#ifdef MOE_TRACE
+#define MOE_WCLK() clock64()
+#define MOE_WADD(var, t0) (var) += clock64() - (t0)
+#else
+#define MOE_WCLK() 0ll
+#define MOE_WADD(var, t0) (void)0
+#endif
+
+template <int MODE>
+struct WCfg;
+template <>
+struct WCfg<1> {
+  static constexpr int KB = kKB1;
+  static constexpr int NT = kNT1;     // 16 pair tiles
+  static constexpr int ROWS = 128;    // token rows per tile
+};
+template <>
+struct WCfg<2> {
+  static constexpr int KB = kKB2;
+  static constexpr int NT = kH / 256; // 28 feature tiles of 256
+  static constexpr int ROWS = 64;
+};
+
+constexpr int kWStages = 4;
+constexpr int kWStageBytes = 3 * 16384;
+constexpr int kWThreads = 320;
+constexpr int kWEpiThreads = 256;
+
+struct WideSmem {
+  uint8_t stage[kWStages][kWStageBytes];
+  uint64_t full[kWStages];
+  uint64_t empty[kWStages];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+  int flag;
+  float ssw[2][kKB1];      // this segment's weight scales (MODE 1: X1, X2 blocks)
+  float amx[2][128];       // MODE 1: per-row amax of each column half
+  int rflag[64];           // MODE 2: per-token last-contributor flags
+  int e_cnt[kEG + 1];
+  int e_start[kEG + 1];
+  int e_tiles[kEG + 1];
+};
+
+constexpr size_t kWideSmemBytes = sizeof(WideSmem) + 1024;
+
+struct WTile {
+  int e, nt, row0, nr;
+};
+
+template <int MODE>
+__device__ __forceinline__ WTile w_decode(const WideSmem& sm, int E, int tile) {
+  constexpr int NT = WCfg<MODE>::NT, ROWS = WCfg<MODE>::ROWS;
+  int lo = 0, hi = E - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (sm.e_tiles[mid] * NT <= tile) lo = mid; else hi = mid - 1;
+  }
+  const int v = tile - sm.e_tiles[lo] * NT;
+  const int jt = sm.e_tiles[lo + 1] - sm.e_tiles[lo];
+  WTile s;
+  s.e = lo;
+  s.nt = v / jt;
+  const int j = v - s.nt * jt;
+  s.row0 = sm.e_start[lo] + ROWS * j;
+  s.nr = min(ROWS, sm.e_cnt[lo] - ROWS * j);
+  return s;
+}
+
+__device__ __forceinline__ float w_silu(float x) { return x / (1.0f + expf(-x)); }
+
+__device__ __forceinline__ uint32_t bf16x2_bits(float lo, float hi) {
+  __nv_bfloat162 b = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&b);
+}
+
+template <int MODE>
+__device__ void w_producer(WideSmem& sm, const CUtensorMap* tmA, const CUtensorMap* tmA2,
+                           const CUtensorMap* tmB, const TileArgs& g, const Sched& sk) {
+  uint32_t stage = 0, phase = 0, issued = 0, lastpar = 0;
+  long long tw = 0, nkb = 0;
+  // MODE 2: the first stages get their weight tiles before the dependency on GEMM1 resolves
+  int pend_n = 0;
+  int pend_row0[kWStages];
+  int pend_kb[kWStages];
+  bool waited = MODE == 1;
+  SegIter it(sk, blockIdx.x);
+  int tile, k0, k1;
+  while (it.next(tile, k0, k1)) {
+    const WTile s = w_decode<MODE>(sm, g.E, tile);
+    for (int kb = k0; kb < k1; ++kb) {
+      const long long t0 = MOE_WCLK();
+      if (!mbar_wait(&sm.empty[stage], phase ^ 1u, &sm.abort, g.status, kStWaitProducer)) goto drain;
+      MOE_WADD(tw, t0);
+      ++nkb;
+      mbar_arrive_expect_tx(&sm.full[stage], kWStageBytes);
+      uint8_t* st = sm.stage[stage];
+      if (MODE == 1) {
+        tma_load_2d(st, tmA, &sm.full[stage], kb * kBlk, s.row0);
+        tma_load_2d(st + 16384, tmB, &sm.full[stage], kb * kBlk, s.e * kN1 + s.nt * kBlk);
+        tma_load_2d(st + 32768, tmB, &sm.full[stage], kb * kBlk, s.e * kN1 + kI + s.nt * kBlk);
+      } else {
+        tma_load_2d(st + 16384, tmB, &sm.full[stage], kb * kBlk, s.e * kH + s.nt * 256);
+        tma_load_2d(st + 32768, tmB, &sm.full[stage], kb * kBlk, s.e * kH + s.nt * 256 + 128);
+        if (!waited) {
+          pend_row0[pend_n] = s.row0;
+          pend_kb[pend_n] = kb;
+          ++pend_n;
+        } else {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            tma_load_2d(st + q * 4096, tmA, &sm.full[stage], kb * kBlk, s.row0 + 16 * q);
+            tma_load_2d(st + q * 4096 + 2048, tmA2, &sm.full[stage], kb * kBlk, s.row0 + 16 * q);
+          }
+        }
+      }
+      issued |= 1u << stage;
+      lastpar = (lastpar & ~(1u << stage)) | (phase << stage);
+      if (++stage == kWStages) {
+        stage = 0;
+        phase ^= 1u;
+      }
+      if (MODE == 2 && !waited && pend_n == kWStages) {
+        pdl_wait();
+        waited = true;
+        for (int i = 0; i < pend_n; ++i)
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            tma_load_2d(sm.stage[i] + q * 4096, tmA, &sm.full[i], pend_kb[i] * kBlk, pend_row0[i] + 16 * q);
+            tma_load_2d(sm.stage[i] + q * 4096 + 2048, tmA2, &sm.full[i], pend_kb[i] * kBlk,
+                        pend_row0[i] + 16 * q);
+          }
+        pend_n = 0;
+      }
+    }
+  }
+  if (MODE == 2 && !waited) {
+    pdl_wait();
+    for (int i = 0; i < pend_n; ++i)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        tma_load_2d(sm.stage[i] + q * 4096, tmA, &sm.full[i], pend_kb[i] * kBlk, pend_row0[i] + 16 * q);
+        tma_load_2d(sm.stage[i] + q * 4096 + 2048, tmA2, &sm.full[i], pend_kb[i] * kBlk, pend_row0[i] + 16 * q);
+      }
+  }
+drain:
+  for (int s = 0; s < kWStages; ++s)
+    if ((issued >> s) & 1u) {
+      int no_abort = 0;
+      mbar_wait(&sm.full[s], (lastpar >> s) & 1u, &no_abort, g.status, kStWaitDrain);
+    }
+#ifdef MOE_TRACE
+  g.trace[blockIdx.x * kTraceSlots + 2] = tw;
+  g.trace[blockIdx.x * kTraceSlots + 3] = nkb;
+#endif
+}
+
+__device__ void w_mma(WideSmem& sm, uint32_t tmem, const TileArgs& g, const Sched& sk) {
+  constexpr uint32_t idesc = idesc_e4m3_f32(128, 256);
+  uint32_t stage = 0, phase = 0, tk = 0, buf = 0;
+  long long tw_t = 0, tw_f = 0, t_first = 0;
+  SegIter it(sk, blockIdx.x);
+  int tile, k0, k1;
+  while (it.next(tile, k0, k1)) {
+    for (int kb = k0; kb < k1; ++kb) {
+      long long t0 = MOE_WCLK();
+      if (!mbar_wait(&sm.tempty[buf], ((tk >> buf) & 1u) ^ 1u, &sm.abort, g.status, kStWaitMmaTmem))
+        goto done;
+      MOE_WADD(tw_t, t0);
+      t0 = MOE_WCLK();
+      if (!mbar_wait(&sm.full[stage], phase, &sm.abort, g.status, kStWaitMma)) goto done;
+      MOE_WADD(tw_f, t0);
+#ifdef MOE_TRACE
+      if (t_first == 0) t_first = static_cast<long long>(globaltimer_ns());
+#endif
+      tc_fence_after();
+      {
+        const uint32_t st = smem_u32(sm.stage[stage]);
+        const uint32_t d = tmem + buf * 256u;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          mma_f8f6f4(d, sdesc_k128_sw128(st + 32 * k), sdesc_k128_sw128(st + 16384 + 32 * k), idesc, k > 0);
+      }
+      mma_commit(&sm.empty[stage]);
+      mma_commit(&sm.tfull[buf]);
+      tk ^= 1u << buf;
+      buf ^= 1u;
+      if (++stage == kWStages) {
+        stage = 0;
+        phase ^= 1u;
+      }
+    }
+  }
+done:
+  mma_commit(&sm.drain);
+  int no_abort = 0;
+  mbar_wait(&sm.drain, 0, &no_abort, g.status, kStWaitDrain);
+#ifdef MOE_TRACE
+  g.trace[blockIdx.x * kTraceSlots + 4] = tw_f;
+  g.trace[blockIdx.x * kTraceSlots + 5] = tw_t;
+  g.trace[blockIdx.x * kTraceSlots + 11] = t_first;
+#endif
+}
+
+// MODE 1 tile epilogue: SwiGLU of this thread's 64 (X1, X2) column pairs of row `rit`, the row's
+// 128-column amax (exchanged with the other column half), hi/lo e4m3 encoding and stores.
+__device__ __forceinline__ void w_epi1(WideSmem& sm, const TileArgs& g, const WTile& s, float* x1,
+                                       const float* x2, int h, int rit) {
+  float amax = 0.f;
+#pragma unroll
+  for (int j = 0; j < 64; ++j) {
+    x1[j] = w_silu(x2[j]) * x1[j];
+    amax = fmaxf(amax, fabsf(x1[j]));
+  }
+  sm.amx[h][rit] = amax;
+  named_bar_sync(1, kWEpiThreads);
+  amax = fmaxf(sm.amx[0][rit], sm.amx[1][rit]);
+  if (rit >= s.nr) return;
+  const size_t row = static_cast<size_t>(s.row0 + rit);
+  const float inv = amax > 0.f ? 448.0f / amax : 0.f;
+  uint32_t hw[16], lw[16];
+#pragma unroll
+  for (int j = 0; j < 64; j += 4) {
+    const float y0 = x1[j] * inv, y1 = x1[j + 1] * inv, y2 = x1[j + 2] * inv, y3 = x1[j + 3] * inv;
+    const uint32_t h01 = cvt_e4m3x2(y0, y1), h23 = cvt_e4m3x2(y2, y3);
+    const float2 b01 = e4m3x2_to_f2(static_cast<uint16_t>(h01));
+    const float2 b23 = e4m3x2_to_f2(static_cast<uint16_t>(h23));
+    const uint32_t l01 = cvt_e4m3x2((y0 - b01.x) * 16.f, (y1 - b01.y) * 16.f);
+    const uint32_t l23 = cvt_e4m3x2((y2 - b23.x) * 16.f, (y3 - b23.y) * 16.f);
+    hw[j / 4] = h01 | (h23 << 16);
+    lw[j / 4] = l01 | (l23 << 16);
+  }
+  const size_t off = row * kI + static_cast<size_t>(s.nt) * kBlk + 64 * h;
+  uint4* dh = reinterpret_cast<uint4*>(g.c_hi + off);
+  uint4* dl = reinterpret_cast<uint4*>(g.c_lo + off);
+#pragma unroll
+  for (int v = 0; v < 4; ++v) {
+    dh[v] = make_uint4(hw[4 * v], hw[4 * v + 1], hw[4 * v + 2], hw[4 * v + 3]);
+    dl[v] = make_uint4(lw[4 * v], lw[4 * v + 1], lw[4 * v + 2], lw[4 * v + 3]);
+  }
+  if (h == 0) g.c_scale[static_cast<size_t>(s.nt) * g.r_pad + row] = amax > 0.f ? amax / 448.0f : 1.0f;
+}
+
+// MODE 2 tile epilogue: hi + lo, then the routing-weighted, expert-ordered combine of this
+// thread's 128 output columns of token `tok` (lanes 0..15 of each quarter).
+__device__ __forceinline__ void w_epi2(WideSmem& sm, const TileArgs& g, const WTile& s, float* acc, int h,
+                                       int q, int lane) {
+#pragma unroll
+  for (int j = 0; j < 128; ++j) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], 16);
+  const int tok = 16 * q + (lane & 15);
+  const bool mine = lane < 16 && tok < s.nr;
+  const int row = s.row0 + tok;
+  int t = 0, kt = 0;
+  float w = 0.f;
+  if (mine) {
+    t = __ldg(g.row_token + row);
+    w = __ldg(g.row_weight + row);
+    kt = __ldg(g.tok_nloc + t);
+  }
+  const int col0 = s.nt * 256 + 128 * h;
+  if (mine) {
+    if (kt == 1) {
+      uint4* o = reinterpret_cast<uint4*>(g.out + static_cast<size_t>(t) * kH + col0);
+#pragma unroll
+      for (int v = 0; v < 16; ++v)
+        o[v] = make_uint4(bf16x2_bits(__fmul_rn(acc[8 * v], w), __fmul_rn(acc[8 * v + 1], w)),
+                          bf16x2_bits(__fmul_rn(acc[8 * v + 2], w), __fmul_rn(acc[8 * v + 3], w)),
+                          bf16x2_bits(__fmul_rn(acc[8 * v + 4], w), __fmul_rn(acc[8 * v + 5], w)),
+                          bf16x2_bits(__fmul_rn(acc[8 * v + 6], w), __fmul_rn(acc[8 * v + 7], w)));
+    } else {
+      float4* p = reinterpret_cast<float4*>(g.part2 + static_cast<size_t>(row) * kH + col0);
+#pragma unroll
+      for (int v = 0; v < 32; ++v) p[v] = make_float4(acc[4 * v], acc[4 * v + 1], acc[4 * v + 2], acc[4 * v + 3]);
+    }
+  }
+  named_bar_sync(1, kWEpiThreads);
+  if (h == 0 && lane < 16) {
+    int fl = 0;
+    if (mine && kt > 1) {
+      int* ctr = g.cnt2 + static_cast<size_t>(t) * WCfg<2>::NT + s.nt;
+      const int prev = atomic_add_acq_rel_gpu(ctr, 1);
+      if (prev == kt - 1) {
+        *ctr = 0;   // last contributor: reset for the next call
+        fl = 1;
+      }
+    }
+    sm.rflag[tok] = fl;
+  }
+  named_bar_sync(1, kWEpiThreads);
+  if (!mine || !sm.rflag[tok]) return;
+  int ra[kTopK];
+  float wa[kTopK];
+#pragma unroll
+  for (int a = 0; a < kTopK; ++a) ra[a] = a < kt ? __ldg(g.tok_rows + static_cast<size_t>(t) * kTopK + a) : 0;
+#pragma unroll
+  for (int a = 0; a < kTopK; ++a) wa[a] = a < kt ? __ldg(g.row_weight + ra[a]) : 0.f;
+  uint4* o = reinterpret_cast<uint4*>(g.out + static_cast<size_t>(t) * kH + col0);
+#pragma unroll 1
+  for (int c0 = 0; c0 < 128; c0 += 32) {   // 32 columns at a time, summed in ascending expert order
+    float sum[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) sum[j] = 0.f;
+#pragma unroll
+    for (int a = 0; a < kTopK; ++a) {
+      if (a >= kt) break;
+      const float4* p = reinterpret_cast<const float4*>(g.part2 + static_cast<size_t>(ra[a]) * kH + col0 + c0);
+#pragma unroll
+      for (int v = 0; v < 8; ++v) {
+        const float4 x = __ldcg(p + v);
+        sum[4 * v] = __fadd_rn(sum[4 * v], __fmul_rn(x.x, wa[a]));
+        sum[4 * v + 1] = __fadd_rn(sum[4 * v + 1], __fmul_rn(x.y, wa[a]));
+        sum[4 * v + 2] = __fadd_rn(sum[4 * v + 2], __fmul_rn(x.z, wa[a]));
+        sum[4 * v + 3] = __fadd_rn(sum[4 * v + 3], __fmul_rn(x.w, wa[a]));
+      }
+    }
+#pragma unroll
+    for (int v = 0; v < 4; ++v)
+      o[c0 / 8 + v] = make_uint4(bf16x2_bits(sum[8 * v], sum[8 * v + 1]), bf16x2_bits(sum[8 * v + 2], sum[8 * v + 3]),
+                                 bf16x2_bits(sum[8 * v + 4], sum[8 * v + 5]), bf16x2_bits(sum[8 * v + 6], sum[8 * v + 7]));
+  }
+}
+
+template <int MODE>
+__device__ void w_epilogue(WideSmem& sm, uint32_t tmem, const TileArgs& g, const Sched& sk, int warp, int lane) {
+  constexpr int KB = WCfg<MODE>::KB;
+  const int ew = warp - 2;
+  const int q = warp & 3;
+  const int h = ew >> 2;
+  const int rit = q * 32 + lane;
+  const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
+  uint32_t tk = 0, buf = 0;
+  bool dead = false;
+  long long tw = 0, tp = 0, te = 0, tf = 0, ts = 0;
+  if (MODE == 2) pdl_wait();   // the C scales and the combine inputs come from GEMM1
+  SegIter it(sk, blockIdx.x);
+  int tile, k0, k1;
+  while (it.next(tile, k0, k1)) {
+    const WTile s = w_decode<MODE>(sm, g.E, tile);
+    long long t0 = MOE_WCLK();
+    // this thread's token row (MODE 2: lanes l and l+16 share token 16q + (l & 15))
+    const int trow = MODE == 1 ? rit : 16 * q + (lane & 15);
+    const size_t srow = static_cast<size_t>(s.row0 + min(trow, s.nr - 1));
+    const float lo_scale = (MODE == 2 && lane >= 16) ? 0.0625f : 1.0f;
+    const float* swp1;
+    const float* swp2;
+    if (MODE == 1) {
+      swp1 = g.sw + (static_cast<size_t>(s.e) * 32 + s.nt) * kKB1;
+      swp2 = g.sw + (static_cast<size_t>(s.e) * 32 + kNT1 + s.nt) * kKB1;
+    } else {
+      swp1 = g.sw + (static_cast<size_t>(s.e) * kNT2 + 2 * s.nt) * kKB2;        // features [256nt, +128)
+      swp2 = g.sw + (static_cast<size_t>(s.e) * kNT2 + 2 * s.nt + 1) * kKB2;    // features [256nt+128, +128)
+    }
+    if (ew == 0)
+      for (int i = lane; i < k1 - k0; i += 32) {
+        sm.ssw[0][i] = __ldg(swp1 + k0 + i);
+        sm.ssw[1][i] = __ldg(swp2 + k0 + i);
+      }
+    // the row's token scales, four K-blocks ahead
+    float pf0 = __ldg(g.sa + static_cast<size_t>(k0) * g.r_pad + srow);
+    float pf1 = k0 + 1 < k1 ? __ldg(g.sa + static_cast<size_t>(k0 + 1) * g.r_pad + srow) : 0.f;
+    float pf2 = k0 + 2 < k1 ? __ldg(g.sa + static_cast<size_t>(k0 + 2) * g.r_pad + srow) : 0.f;
+    float pf3 = k0 + 3 < k1 ? __ldg(g.sa + static_cast<size_t>(k0 + 3) * g.r_pad + srow) : 0.f;
+    named_bar_sync(1, kWEpiThreads);
+    MOE_WADD(ts, t0);
+    float acc1[MODE == 1 ? 64 : 128], acc2[MODE == 1 ? 64 : 1];
+#pragma unroll
+    for (int j = 0; j < (MODE == 1 ? 64 : 128); ++j) acc1[j] = 0.f;
+#pragma unroll
+    for (int j = 0; j < (MODE == 1 ? 64 : 1); ++j) acc2[j] = 0.f;
+    for (int kb = k0; kb < k1; ++kb) {
+      const int ki = kb - k0;
+      const float sa = pf0;
+      pf0 = pf1;
+      pf1 = pf2;
+      pf2 = pf3;
+      pf3 = kb + 4 < k1 ? __ldg(g.sa + static_cast<size_t>(kb + 4) * g.r_pad + srow) : 0.f;
+      t0 = MOE_WCLK();
+      if (!dead && !mbar_wait(&sm.tfull[buf], (tk >> buf) & 1u, &sm.abort, g.status, kStWaitEpilogue))
+        dead = true;
+      MOE_WADD(tw, t0);
+      t0 = MOE_WCLK();
+      if (!dead) {
+        tc_fence_after();
+        const uint32_t base = lane_base + buf * 256u;
+        if (MODE == 1) {
+          const float f1 = sa * sm.ssw[0][ki], f2 = sa * sm.ssw[1][ki];
+#pragma unroll
+          for (int c0 = 0; c0 < 64; c0 += 16) {
+            float d1[16], d2[16];
+            tmem_ld16x2_wait(base + 64u * h + c0, base + 128u + 64u * h + c0, d1, d2);
+            if (c0 == 48) {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&sm.tempty[buf]);
+            }
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              acc1[c0 + j] = fmaf(d1[j], f1, acc1[c0 + j]);
+              acc2[c0 + j] = fmaf(d2[j], f2, acc2[c0 + j]);
+            }
+          }
+        } else {
+          const float f = sa * sm.ssw[h][ki] * lo_scale;
+#pragma unroll
+          for (int c0 = 0; c0 < 128; c0 += 32) {
+            float d1[16], d2[16];
+            tmem_ld16x2_wait(base + 128u * h + c0, base + 128u * h + c0 + 16u, d1, d2);
+            if (c0 == 96) {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&sm.tempty[buf]);
+            }
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              acc1[c0 + j] = fmaf(d1[j], f, acc1[c0 + j]);
+              acc1[c0 + 16 + j] = fmaf(d2[j], f, acc1[c0 + 16 + j]);
+            }
+          }
+        }
+      }
+      MOE_WADD(tp, t0);
+      tk ^= 1u << buf;
+      buf ^= 1u;
+    }
+    t0 = MOE_WCLK();
+    if (!(k0 == 0 && k1 == KB)) {
+      // stream-K fixup: publish this CTA's partial; the last contributor sums them in CTA order.
+      // Slot layout [256 columns][128 rows] (MODE 1 columns: X1 0..127, X2 128..255).
+      const int slot = sk.slot(blockIdx.x, tile);
+      float* p = g.part + static_cast<size_t>(slot) * 256 * 128;
+      if (MODE == 1) {
+#pragma unroll
+        for (int j = 0; j < 64; ++j) {
+          p[(64 * h + j) * 128 + rit] = acc1[j];
+          p[(128 + 64 * h + j) * 128 + rit] = acc2[j];
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 128; ++j) p[(128 * h + j) * 128 + rit] = acc1[j];
+      }
+      named_bar_sync(1, kWEpiThreads);
+      if (ew == 0 && lane == 0) {
+        const int expect = sk.last_cta(tile) - sk.first_cta(tile) + 1;
+        const int prev = atomic_add_acq_rel_gpu(g.tile_cnt + tile, 1);
+        const int last = prev == expect - 1;
+        if (last) g.tile_cnt[tile] = 0;
+        sm.flag = last;
+      }
+      named_bar_sync(1, kWEpiThreads);
+      const int last = sm.flag;
+      named_bar_sync(1, kWEpiThreads);
+      if (!last) {
+        MOE_WADD(tf, t0);
+        continue;
+      }
+#pragma unroll
+      for (int j = 0; j < (MODE == 1 ? 64 : 128); ++j) acc1[j] = 0.f;
+#pragma unroll
+      for (int j = 0; j < (MODE == 1 ? 64 : 1); ++j) acc2[j] = 0.f;
+      for (int cta = sk.first_cta(tile); cta <= sk.last_cta(tile); ++cta) {
+        const float* pp = g.part + static_cast<size_t>(sk.slot(cta, tile)) * 256 * 128;
+        if (MODE == 1) {
+#pragma unroll
+          for (int j = 0; j < 64; ++j) {
+            acc1[j] += __ldcg(pp + (64 * h + j) * 128 + rit);
+            acc2[j] += __ldcg(pp + (128 + 64 * h + j) * 128 + rit);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 128; ++j) acc1[j] += __ldcg(pp + (128 * h + j) * 128 + rit);
+        }
+      }
+    }
+    MOE_WADD(tf, t0);
+    t0 = MOE_WCLK();
+    // (after an abort the epilogue still runs, on garbage, so every warp meets every barrier)
+    if (MODE == 1)
+      w_epi1(sm, g, s, acc1, acc2, h, rit);
+    else
+      w_epi2(sm, g, s, acc1, h, q, lane);
+    MOE_WADD(te, t0);
+  }
+#ifdef MOE_TRACE
+  if (warp == 2 && lane == 0) {
+    unsigned long long* tr = g.trace + blockIdx.x * kTraceSlots;
+    tr[6] = tw;
+    tr[7] = tp;
+    tr[8] = te;
+    tr[9] = tf;
+    tr[10] = ts;
+    tr[1] = globaltimer_ns();
+  }
+#endif
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kWThreads, 1)
+    wide_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA2,
+                const __grid_constant__ CUtensorMap tmB, TileArgs g) {
+  extern __shared__ uint8_t smem_raw[];
+  WideSmem& sm = *reinterpret_cast<WideSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  if (MODE == 1) {
+    pdl_wait();
+    pdl_launch_dependents();
+  }
+  const Plan plan = *g.plan;
+  const int ntiles = (MODE == 1 ? plan.m_tiles : plan.m64) * WCfg<MODE>::NT;
+  Sched sk;
+  sk.init(ntiles, gridDim.x, WCfg<MODE>::KB);
+  if (ntiles == 0 || !sk.has_work(blockIdx.x)) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i <= g.E; i += blockDim.x) {
+    sm.e_cnt[i] = i < g.E ? g.e_count[i] : 0;
+    sm.e_start[i] = g.e_start[i];
+    sm.e_tiles[i] = g.e_tiles[i];
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kWStages; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sm.tfull[b], 1);
+      mbar_init(&sm.tempty[b], 8);
+    }
+    mbar_init(&sm.drain, 1);
+    sm.abort = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmA2);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(&sm.tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+#ifdef MOE_TRACE
+  if (threadIdx.x == 0) g.trace[blockIdx.x * kTraceSlots + 0] = globaltimer_ns();
+#endif
+  const uint32_t tmem = sm.tmem_base;
+  if (warp == 0) {
+    if (lane == 0) w_producer<MODE>(sm, &tmA, &tmA2, &tmB, g, sk);
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) w_mma(sm, tmem, g, sk);
+    __syncwarp();
+  } else {
+    w_epilogue<MODE>(sm, tmem, g, sk, warp, lane);
+    __syncwarp();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+cudaError_t wide_prepare() {
+  cudaError_t e = cudaFuncSetAttribute(wide_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(kWideSmemBytes));
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(wide_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(kWideSmemBytes));
+}
+
+// Launched as programmatic dependents of the preceding kernel in the stream (PDL).
+cudaError_t wide_launch(int mode, int grid, cudaStream_t st, const CUtensorMap& a, const CUtensorMap& a2,
+                        const CUtensorMap& b, const TileArgs& g) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kWThreads);
+  cfg.dynamicSmemBytes = kWideSmemBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (mode == 1) return cudaLaunchKernelEx(&cfg, wide_kernel<1>, a, a2, b, g);
+  return cudaLaunchKernelEx(&cfg, wide_kernel<2>, a, a2, b, g);
+}
+
+}  // namespace moe

@@ -183,3 +183,31 @@ def test_empty_batch(cuda_device):
     x["hidden_states_scale"] = x["hidden_states_scale"][:, :0].contiguous()
     out = M.run(**x)
     assert out.shape == (0, 7168)
+
+
+@pytest.mark.parametrize("T,E,offset", [(200, 8, 0), (600, 8, 16)])
+def test_every_token_on_eight_local_experts(cuda_device, T, E, offset):
+    """Steered routing puts all 8 picks of every token on local experts, so every output row
+    is the expert-ordered combine of 8 partial rows (streaming path at T=200, wide at T=600)."""
+    from moe_swarm_b200 import workload as W
+    favour = list(range(8))
+    x = W.make_steered_activations(T, 81 + T, offset, favour)
+    x.update(W.make_weights(E, offset, 81 + T))
+    x["local_expert_offset"] = offset
+    x["routed_scaling_factor"] = 2.5
+    d = C.to_device(x, cuda_device)
+    out = M.run(**d)
+    torch.cuda.synchronize()
+    _status_ok(cuda_device)
+    _expect_parity(out, O.run(**x), f"T={T} E={E} steered")
+
+
+def test_wide_path_T1500(cuda_device):
+    """T above the streaming threshold with 32 local experts at offset 32."""
+    x = C.make_case(1500, 91, offset=32)
+    d = C.to_device(x, cuda_device)
+    out = M.run(**d)
+    torch.cuda.synchronize()
+    _status_ok(cuda_device)
+    _intermediate_check(d, x, cuda_device)
+    _expect_parity(out, O.run(**x), "T=1500")
