@@ -21,6 +21,8 @@ cudaError_t wide_prepare();
 cudaError_t wide_launch(int mode, int grid, cudaStream_t st, const CUtensorMap& a, const CUtensorMap& a2,
                         const CUtensorMap& b, const TileArgs& g);
 cudaError_t stream_prepare();
+cudaError_t combine_launch(int T, int grid, cudaStream_t st, const int* tok_nloc, const int* tok_rows,
+                           const float* part2, uint16_t* out);
 cudaError_t stream_launch(int mode, int grid, cudaStream_t st, const CUtensorMap& w, const CUtensorMap& t,
                           const CUtensorMap& t2, const TileArgs& g);
 
@@ -237,6 +239,18 @@ struct moe_b200_timer {
 
 namespace {
 
+int launch_combine(const moe_b200_args* a, uint8_t* ws, const moe::Layout& L, int sms, cudaStream_t st,
+                   int* launches) {
+  const int T = a->num_tokens;
+  const int grid = T < 8 * sms ? T : 8 * sms;
+  cudaError_t e = moe::combine_launch(T, grid, st, reinterpret_cast<const int*>(ws + L.tok_nloc),
+                                      reinterpret_cast<const int*>(ws + L.tok_rows),
+                                      reinterpret_cast<const float*>(ws + L.part2), a->output);
+  if (e != cudaSuccess) return cuda_fail(e, "combine launch");
+  ++*launches;
+  return MOE_B200_OK;
+}
+
 moe::TileArgs tile_args(const moe_b200_args* a, uint8_t* ws, const moe::Layout& L) {
   moe::TileArgs s{};
   s.plan = reinterpret_cast<const moe::Plan*>(ws + L.plan);
@@ -324,6 +338,8 @@ int forward_impl(const moe_b200_args* a, void* workspace, size_t ws_bytes, void*
     e = moe::stream_launch(2, grid, st, mW2s, mHi, mLo, s2);
     if (e != cudaSuccess) return cuda_fail(e, "stream gemm2 launch");
     ++launches;
+    rc = launch_combine(a, ws, L, di.sms, st, &launches);
+    if (rc) return rc;
     if (ev) cudaEventRecord(ev[3], st);
     g_last_launches = launches;
     return MOE_B200_OK;
@@ -356,6 +372,8 @@ int forward_impl(const moe_b200_args* a, void* workspace, size_t ws_bytes, void*
   e = moe::wide_launch(2, grid, st, mChi, mClo, mW2, w2);
   if (e != cudaSuccess) return cuda_fail(e, "wide gemm2 launch");
   ++launches;
+  rc = launch_combine(a, ws, L, di.sms, st, &launches);
+  if (rc) return rc;
   if (ev) cudaEventRecord(ev[3], st);
   g_last_launches = launches;
   return MOE_B200_OK;

@@ -1,0 +1,62 @@
+// Expert-ordered combine of tokens routed to more than one local expert:
+//   out[t, :] = bf16( sum over t's local experts, ascending, of w_e * O_e[t, :] )
+// where the GEMM2 kernels left each w_e * O_e row in fp32 in the partial-row buffer.  This is
+// the accumulation order of the reference's per-expert index_add_
+// (spec/reference_official.py:134-166), so the result is deterministic.  Tokens with one local
+// expert were written by GEMM2 directly and tokens with none by the routing kernel.
+#include <cuda_bf16.h>
+
+#include "launch_args.cuh"
+#include "moe_internal.cuh"
+#include "ptx.cuh"
+
+namespace moe {
+
+constexpr int kCombineThreads = 256;
+
+__global__ void __launch_bounds__(kCombineThreads) combine_kernel(const int* tok_nloc, const int* tok_rows,
+                                                                  const float* part2, uint16_t* out, int T) {
+  pdl_wait();   // the partial rows come from GEMM2
+  for (int t = blockIdx.x; t < T; t += gridDim.x) {
+    const int kt = __ldg(tok_nloc + t);
+    if (kt <= 1) continue;
+    int rows[kTopK];
+#pragma unroll
+    for (int a = 0; a < kTopK; ++a) rows[a] = a < kt ? __ldg(tok_rows + static_cast<size_t>(t) * kTopK + a) : 0;
+    for (int v = threadIdx.x; v < kH / 4; v += kCombineThreads) {
+      float4 x[kTopK];
+#pragma unroll
+      for (int a = 0; a < kTopK; ++a)
+        if (a < kt) x[a] = __ldcg(reinterpret_cast<const float4*>(part2 + static_cast<size_t>(rows[a]) * kH) + v);
+      float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int a = 0; a < kTopK; ++a)
+        if (a < kt) {
+          s.x = __fadd_rn(s.x, x[a].x);
+          s.y = __fadd_rn(s.y, x[a].y);
+          s.z = __fadd_rn(s.z, x[a].z);
+          s.w = __fadd_rn(s.w, x[a].w);
+        }
+      __nv_bfloat162 lo = __floats2bfloat162_rn(s.x, s.y), hi = __floats2bfloat162_rn(s.z, s.w);
+      uint2 pk = make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+      *reinterpret_cast<uint2*>(out + static_cast<size_t>(t) * kH + 4 * v) = pk;
+    }
+  }
+}
+
+// Launched as a programmatic dependent of GEMM2.
+cudaError_t combine_launch(int T, int grid, cudaStream_t st, const int* tok_nloc, const int* tok_rows,
+                           const float* part2, uint16_t* out) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kCombineThreads);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, combine_kernel, tok_nloc, tok_rows, part2, out, T);
+}
+
+}  // namespace moe

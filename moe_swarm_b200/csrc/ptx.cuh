@@ -258,6 +258,20 @@ __device__ __forceinline__ void warp_colmax32(float* v, int lane) {
   }
 }
 
+// Per-warpgroup register reallocation (executed by all 128 threads of the warpgroup).
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+// silu(x) = x / (1 + exp(-x)) with the fast exponential and divide intrinsics (the result
+// feeds an 8-bit-mantissa encoding; their few-ulp error is far below it).
+__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+
 // ---------------------------------------------------------------- misc
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");

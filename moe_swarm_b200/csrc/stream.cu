@@ -82,7 +82,6 @@ struct StreamSmem {
   uint32_t tmem_base;
   int abort;
   int flag;
-  int colflag[kTok];
   int col_t[kTok];
   int col_k[kTok];
   float col_w[kTok];
@@ -121,7 +120,7 @@ __device__ __forceinline__ STile s_decode(const StreamSmem<MODE>& sm, int E, int
   return s;
 }
 
-__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
+__device__ __forceinline__ float silu_f(float x) { return silu_fast(x); }
 
 __device__ __forceinline__ uint16_t bf16_bits(float v) {
   __nv_bfloat16 b = __float2bfloat16_rn(v);
@@ -308,7 +307,8 @@ __device__ void s_epi1(StreamSmem<1>& sm, const TileArgs& g, const STile& s, flo
   named_bar_sync(1, kSEpiThreads);
 }
 
-// MODE 2 tile epilogue: routing-weighted, expert-ordered combine into the bf16 output.
+// MODE 2 tile epilogue: for each token column, the bf16 output row directly when the token
+// has one local expert, otherwise the routing-weighted fp32 row for the combine kernel.
 __device__ void s_epi2(StreamSmem<2>& sm, const TileArgs& g, const STile& s, const float* acc, int q,
                        int lane) {
   const int r = q * 32 + lane;
@@ -329,49 +329,12 @@ __device__ void s_epi2(StreamSmem<2>& sm, const TileArgs& g, const STile& s, con
 #pragma unroll
   for (int c = 0; c < kTok; ++c) {
     if (c >= s.nr) break;
-    const int t = sm.col_t[c];
+    const float v = __fmul_rn(acc[c], sm.col_w[c]);
     if (sm.col_k[c] == 1)
-      g.out[static_cast<size_t>(t) * kH + f] = bf16_bits(__fmul_rn(acc[c], sm.col_w[c]));
+      g.out[static_cast<size_t>(sm.col_t[c]) * kH + f] = bf16_bits(v);
     else
-      g.part2[static_cast<size_t>(s.row0 + c) * kH + f] = acc[c];
+      g.part2[static_cast<size_t>(s.row0 + c) * kH + f] = v;
   }
-  named_bar_sync(1, kSEpiThreads);
-  if (q == 0) {
-    int fl = 0;
-    const int kt = sm.col_k[lane];
-    if (lane < s.nr && kt > 1) {
-      int* ctr = g.cnt2 + static_cast<size_t>(sm.col_t[lane]) * kNT2 + s.nt;
-      const int prev = atomic_add_acq_rel_gpu(ctr, 1);
-      if (prev == kt - 1) {
-        *ctr = 0;   // last contributor: reset for the next call
-        fl = 1;
-      }
-    }
-    sm.colflag[lane] = fl;
-  }
-  named_bar_sync(1, kSEpiThreads);
-  for (int c = 0; c < s.nr; ++c) {
-    if (!sm.colflag[c]) continue;
-    const int t = sm.col_t[c];
-    const int kt = sm.col_k[c];
-    int ra[kTopK];
-    float wa[kTopK];
-#pragma unroll
-    for (int a = 0; a < kTopK; ++a) {
-      ra[a] = a < kt ? __ldg(g.tok_rows + static_cast<size_t>(t) * kTopK + a) : 0;
-    }
-#pragma unroll
-    for (int a = 0; a < kTopK; ++a) wa[a] = a < kt ? __ldg(g.row_weight + ra[a]) : 0.f;
-    float o[kTopK];
-#pragma unroll
-    for (int a = 0; a < kTopK; ++a) o[a] = a < kt ? __ldcg(g.part2 + static_cast<size_t>(ra[a]) * kH + f) : 0.f;
-    float sum = 0.f;
-#pragma unroll
-    for (int a = 0; a < kTopK; ++a)
-      if (a < kt) sum = __fadd_rn(sum, __fmul_rn(o[a], wa[a]));
-    g.out[static_cast<size_t>(t) * kH + f] = bf16_bits(sum);
-  }
-  named_bar_sync(1, kSEpiThreads);
 }
 
 template <int MODE>

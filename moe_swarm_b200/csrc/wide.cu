@@ -13,12 +13,13 @@
 //     of 16 so that a token's two rows sit in one TMEM lane quarter: smem/TMEM row
 //     32q + i (i < 16) is hi of token 16q + i, row 32q + 16 + i is lo of the same token.
 //       acc[r][c] += D[r][c] * sc[token(r), kb] * s2[e, nt, kb] * (lo ? 1/16 : 1)
-//     epilogue: one shuffle adds a token's lo half to its hi half; then the routing-weighted,
-//     expert-ordered combine into the bf16 output (direct for a token with one local expert,
-//     else through the per-(token, 256-feature) arrival counter).
+//     epilogue: one shuffle adds a token's lo half to its hi half; a token with one local
+//     expert gets its bf16 output row directly, otherwise w * O goes to its fp32 partial row,
+//     summed in ascending expert order by the combine kernel (combine.cu).
 //
-// CTA = 10 warps: warp 0 TMA producer, warp 1 TMEM owner + single-thread MMA issuer,
-// warps 2..9 promotion/epilogue: two warps per TMEM lane quarter, one per column half.
+// CTA = 12 warps: warp 0 TMA producer, warp 1 TMEM owner + single-thread MMA issuer (their
+// warpgroup drops to 40 registers), warps 4..11 promotion/epilogue with 232 registers: two
+// warps per TMEM lane quarter, one per column half.
 // 4 smem stages of 48 KB, 2 TMEM accumulator buffers of 256 columns.  Work: data-parallel
 // whole tiles, then a stream-K tail (sched.cuh).  No TMA multicast (the kernels also run in the
 // multi-GPU expert-parallel configuration).
@@ -58,7 +59,7 @@ struct WCfg<2> {
 
 constexpr int kWStages = 4;
 constexpr int kWStageBytes = 3 * 16384;
-constexpr int kWThreads = 320;
+constexpr int kWThreads = 384;   // 3 warpgroups: producer/MMA (+2 idle warps), 2 x epilogue
 constexpr int kWEpiThreads = 256;
 
 struct WideSmem {
@@ -73,7 +74,6 @@ struct WideSmem {
   int flag;
   float ssw[2][kKB1];      // this segment's weight scales (MODE 1: X1, X2 blocks)
   float amx[2][128];       // MODE 1: per-row amax of each column half
-  int rflag[64];           // MODE 2: per-token last-contributor flags
   int e_cnt[kEG + 1];
   int e_start[kEG + 1];
   int e_tiles[kEG + 1];
@@ -104,7 +104,7 @@ __device__ __forceinline__ WTile w_decode(const WideSmem& sm, int E, int tile) {
   return s;
 }
 
-__device__ __forceinline__ float w_silu(float x) { return x / (1.0f + expf(-x)); }
+__device__ __forceinline__ float w_silu(float x) { return silu_fast(x); }
 
 __device__ __forceinline__ uint32_t bf16x2_bits(float lo, float hi) {
   __nv_bfloat162 b = __floats2bfloat162_rn(lo, hi);
@@ -112,7 +112,7 @@ __device__ __forceinline__ uint32_t bf16x2_bits(float lo, float hi) {
 }
 
 template <int MODE>
-__device__ void w_producer(WideSmem& sm, const CUtensorMap* tmA, const CUtensorMap* tmA2,
+__device__ __forceinline__ void w_producer(WideSmem& sm, const CUtensorMap* tmA, const CUtensorMap* tmA2,
                            const CUtensorMap* tmB, const TileArgs& g, const Sched& sk) {
   uint32_t stage = 0, phase = 0, issued = 0, lastpar = 0;
   long long tw = 0, nkb = 0;
@@ -192,7 +192,7 @@ drain:
 #endif
 }
 
-__device__ void w_mma(WideSmem& sm, uint32_t tmem, const TileArgs& g, const Sched& sk) {
+__device__ __forceinline__ void w_mma(WideSmem& sm, uint32_t tmem, const TileArgs& g, const Sched& sk) {
   constexpr uint32_t idesc = idesc_e4m3_f32(128, 256);
   uint32_t stage = 0, phase = 0, tk = 0, buf = 0;
   long long tw_t = 0, tw_f = 0, t_first = 0;
@@ -278,89 +278,40 @@ __device__ __forceinline__ void w_epi1(WideSmem& sm, const TileArgs& g, const WT
   if (h == 0) g.c_scale[static_cast<size_t>(s.nt) * g.r_pad + row] = amax > 0.f ? amax / 448.0f : 1.0f;
 }
 
-// MODE 2 tile epilogue: hi + lo, then the routing-weighted, expert-ordered combine of this
-// thread's 128 output columns of token `tok` (lanes 0..15 of each quarter).
-__device__ __forceinline__ void w_epi2(WideSmem& sm, const TileArgs& g, const WTile& s, float* acc, int h,
-                                       int q, int lane) {
+// MODE 2 tile epilogue: hi + lo, then this thread's 128 output columns of token `tok` (lanes
+// 0..15 of each quarter): the bf16 output row directly for a token with one local expert,
+// otherwise the routing-weighted fp32 row for the combine kernel.
+__device__ __forceinline__ void w_epi2(const TileArgs& g, const WTile& s, float* acc, int h, int q, int lane) {
 #pragma unroll
   for (int j = 0; j < 128; ++j) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], 16);
   const int tok = 16 * q + (lane & 15);
-  const bool mine = lane < 16 && tok < s.nr;
+  if (lane >= 16 || tok >= s.nr) return;
   const int row = s.row0 + tok;
-  int t = 0, kt = 0;
-  float w = 0.f;
-  if (mine) {
-    t = __ldg(g.row_token + row);
-    w = __ldg(g.row_weight + row);
-    kt = __ldg(g.tok_nloc + t);
-  }
+  const int t = __ldg(g.row_token + row);
+  const float w = __ldg(g.row_weight + row);
+  const int kt = __ldg(g.tok_nloc + t);
   const int col0 = s.nt * 256 + 128 * h;
-  if (mine) {
-    if (kt == 1) {
-      uint4* o = reinterpret_cast<uint4*>(g.out + static_cast<size_t>(t) * kH + col0);
+  if (kt == 1) {
+    uint4* o = reinterpret_cast<uint4*>(g.out + static_cast<size_t>(t) * kH + col0);
 #pragma unroll
-      for (int v = 0; v < 16; ++v)
-        o[v] = make_uint4(bf16x2_bits(__fmul_rn(acc[8 * v], w), __fmul_rn(acc[8 * v + 1], w)),
-                          bf16x2_bits(__fmul_rn(acc[8 * v + 2], w), __fmul_rn(acc[8 * v + 3], w)),
-                          bf16x2_bits(__fmul_rn(acc[8 * v + 4], w), __fmul_rn(acc[8 * v + 5], w)),
-                          bf16x2_bits(__fmul_rn(acc[8 * v + 6], w), __fmul_rn(acc[8 * v + 7], w)));
-    } else {
-      float4* p = reinterpret_cast<float4*>(g.part2 + static_cast<size_t>(row) * kH + col0);
+    for (int v = 0; v < 16; ++v)
+      o[v] = make_uint4(bf16x2_bits(__fmul_rn(acc[8 * v], w), __fmul_rn(acc[8 * v + 1], w)),
+                        bf16x2_bits(__fmul_rn(acc[8 * v + 2], w), __fmul_rn(acc[8 * v + 3], w)),
+                        bf16x2_bits(__fmul_rn(acc[8 * v + 4], w), __fmul_rn(acc[8 * v + 5], w)),
+                        bf16x2_bits(__fmul_rn(acc[8 * v + 6], w), __fmul_rn(acc[8 * v + 7], w)));
+  } else {
+    float4* p = reinterpret_cast<float4*>(g.part2 + static_cast<size_t>(row) * kH + col0);
 #pragma unroll
-      for (int v = 0; v < 32; ++v) p[v] = make_float4(acc[4 * v], acc[4 * v + 1], acc[4 * v + 2], acc[4 * v + 3]);
-    }
-  }
-  named_bar_sync(1, kWEpiThreads);
-  if (h == 0 && lane < 16) {
-    int fl = 0;
-    if (mine && kt > 1) {
-      int* ctr = g.cnt2 + static_cast<size_t>(t) * WCfg<2>::NT + s.nt;
-      const int prev = atomic_add_acq_rel_gpu(ctr, 1);
-      if (prev == kt - 1) {
-        *ctr = 0;   // last contributor: reset for the next call
-        fl = 1;
-      }
-    }
-    sm.rflag[tok] = fl;
-  }
-  named_bar_sync(1, kWEpiThreads);
-  if (!mine || !sm.rflag[tok]) return;
-  int ra[kTopK];
-  float wa[kTopK];
-#pragma unroll
-  for (int a = 0; a < kTopK; ++a) ra[a] = a < kt ? __ldg(g.tok_rows + static_cast<size_t>(t) * kTopK + a) : 0;
-#pragma unroll
-  for (int a = 0; a < kTopK; ++a) wa[a] = a < kt ? __ldg(g.row_weight + ra[a]) : 0.f;
-  uint4* o = reinterpret_cast<uint4*>(g.out + static_cast<size_t>(t) * kH + col0);
-#pragma unroll 1
-  for (int c0 = 0; c0 < 128; c0 += 32) {   // 32 columns at a time, summed in ascending expert order
-    float sum[32];
-#pragma unroll
-    for (int j = 0; j < 32; ++j) sum[j] = 0.f;
-#pragma unroll
-    for (int a = 0; a < kTopK; ++a) {
-      if (a >= kt) break;
-      const float4* p = reinterpret_cast<const float4*>(g.part2 + static_cast<size_t>(ra[a]) * kH + col0 + c0);
-#pragma unroll
-      for (int v = 0; v < 8; ++v) {
-        const float4 x = __ldcg(p + v);
-        sum[4 * v] = __fadd_rn(sum[4 * v], __fmul_rn(x.x, wa[a]));
-        sum[4 * v + 1] = __fadd_rn(sum[4 * v + 1], __fmul_rn(x.y, wa[a]));
-        sum[4 * v + 2] = __fadd_rn(sum[4 * v + 2], __fmul_rn(x.z, wa[a]));
-        sum[4 * v + 3] = __fadd_rn(sum[4 * v + 3], __fmul_rn(x.w, wa[a]));
-      }
-    }
-#pragma unroll
-    for (int v = 0; v < 4; ++v)
-      o[c0 / 8 + v] = make_uint4(bf16x2_bits(sum[8 * v], sum[8 * v + 1]), bf16x2_bits(sum[8 * v + 2], sum[8 * v + 3]),
-                                 bf16x2_bits(sum[8 * v + 4], sum[8 * v + 5]), bf16x2_bits(sum[8 * v + 6], sum[8 * v + 7]));
+    for (int v = 0; v < 32; ++v)
+      p[v] = make_float4(__fmul_rn(acc[4 * v], w), __fmul_rn(acc[4 * v + 1], w), __fmul_rn(acc[4 * v + 2], w),
+                         __fmul_rn(acc[4 * v + 3], w));
   }
 }
 
 template <int MODE>
-__device__ void w_epilogue(WideSmem& sm, uint32_t tmem, const TileArgs& g, const Sched& sk, int warp, int lane) {
+__device__ __forceinline__ void w_epilogue(WideSmem& sm, uint32_t tmem, const TileArgs& g, const Sched& sk, int warp, int lane) {
   constexpr int KB = WCfg<MODE>::KB;
-  const int ew = warp - 2;
+  const int ew = warp - 4;
   const int q = warp & 3;
   const int h = ew >> 2;
   const int rit = q * 32 + lane;
@@ -421,36 +372,50 @@ __device__ void w_epilogue(WideSmem& sm, uint32_t tmem, const TileArgs& g, const
         const uint32_t base = lane_base + buf * 256u;
         if (MODE == 1) {
           const float f1 = sa * sm.ssw[0][ki], f2 = sa * sm.ssw[1][ki];
+          const float2 f1v = make_float2(f1, f1), f2v = make_float2(f2, f2);
 #pragma unroll
-          for (int c0 = 0; c0 < 64; c0 += 16) {
-            float d1[16], d2[16];
-            tmem_ld16x2_wait(base + 64u * h + c0, base + 128u + 64u * h + c0, d1, d2);
-            if (c0 == 48) {
+          for (int c0 = 0; c0 < 64; c0 += 32) {
+            float d1[32], d2[32];
+            tmem_ld32x2_wait(base + 64u * h + c0, base + 128u + 64u * h + c0, d1, d2);
+            if (c0 == 32) {
               tc_fence_before();
               __syncwarp();
               if (lane == 0) mbar_arrive(&sm.tempty[buf]);
             }
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              acc1[c0 + j] = fmaf(d1[j], f1, acc1[c0 + j]);
-              acc2[c0 + j] = fmaf(d2[j], f2, acc2[c0 + j]);
+            for (int j = 0; j < 32; j += 2) {
+              float2 a1 = make_float2(acc1[c0 + j], acc1[c0 + j + 1]);
+              float2 a2 = make_float2(acc2[c0 + j], acc2[c0 + j + 1]);
+              a1 = __ffma2_rn(make_float2(d1[j], d1[j + 1]), f1v, a1);
+              a2 = __ffma2_rn(make_float2(d2[j], d2[j + 1]), f2v, a2);
+              acc1[c0 + j] = a1.x;
+              acc1[c0 + j + 1] = a1.y;
+              acc2[c0 + j] = a2.x;
+              acc2[c0 + j + 1] = a2.y;
             }
           }
         } else {
           const float f = sa * sm.ssw[h][ki] * lo_scale;
+          const float2 fv = make_float2(f, f);
 #pragma unroll
-          for (int c0 = 0; c0 < 128; c0 += 32) {
-            float d1[16], d2[16];
-            tmem_ld16x2_wait(base + 128u * h + c0, base + 128u * h + c0 + 16u, d1, d2);
-            if (c0 == 96) {
+          for (int c0 = 0; c0 < 128; c0 += 64) {
+            float d1[32], d2[32];
+            tmem_ld32x2_wait(base + 128u * h + c0, base + 128u * h + c0 + 32u, d1, d2);
+            if (c0 == 64) {
               tc_fence_before();
               __syncwarp();
               if (lane == 0) mbar_arrive(&sm.tempty[buf]);
             }
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              acc1[c0 + j] = fmaf(d1[j], f, acc1[c0 + j]);
-              acc1[c0 + 16 + j] = fmaf(d2[j], f, acc1[c0 + 16 + j]);
+            for (int j = 0; j < 32; j += 2) {
+              float2 a1 = make_float2(acc1[c0 + j], acc1[c0 + j + 1]);
+              float2 a2 = make_float2(acc1[c0 + 32 + j], acc1[c0 + 32 + j + 1]);
+              a1 = __ffma2_rn(make_float2(d1[j], d1[j + 1]), fv, a1);
+              a2 = __ffma2_rn(make_float2(d2[j], d2[j + 1]), fv, a2);
+              acc1[c0 + j] = a1.x;
+              acc1[c0 + j + 1] = a1.y;
+              acc1[c0 + 32 + j] = a2.x;
+              acc1[c0 + 32 + j + 1] = a2.y;
             }
           }
         }
@@ -514,11 +479,11 @@ __device__ void w_epilogue(WideSmem& sm, uint32_t tmem, const TileArgs& g, const
     if (MODE == 1)
       w_epi1(sm, g, s, acc1, acc2, h, rit);
     else
-      w_epi2(sm, g, s, acc1, h, q, lane);
+      w_epi2(g, s, acc1, h, q, lane);
     MOE_WADD(te, t0);
   }
 #ifdef MOE_TRACE
-  if (warp == 2 && lane == 0) {
+  if (warp == 4 && lane == 0) {
     unsigned long long* tr = g.trace + blockIdx.x * kTraceSlots;
     tr[6] = tw;
     tr[7] = tp;
@@ -578,13 +543,18 @@ __global__ void __launch_bounds__(kWThreads, 1)
   if (threadIdx.x == 0) g.trace[blockIdx.x * kTraceSlots + 0] = globaltimer_ns();
 #endif
   const uint32_t tmem = sm.tmem_base;
-  if (warp == 0) {
-    if (lane == 0) w_producer<MODE>(sm, &tmA, &tmA2, &tmB, g, sk);
-    __syncwarp();
-  } else if (warp == 1) {
-    if (lane == 0) w_mma(sm, tmem, g, sk);
-    __syncwarp();
+  // 384 threads x 168 registers at launch = 128 x 56 (producer/MMA warpgroup) + 256 x 224
+  if (warp < 4) {
+    setmaxnreg_dec<56>();
+    if (warp == 0) {
+      if (lane == 0) w_producer<MODE>(sm, &tmA, &tmA2, &tmB, g, sk);
+      __syncwarp();
+    } else if (warp == 1) {
+      if (lane == 0) w_mma(sm, tmem, g, sk);
+      __syncwarp();
+    }
   } else {
+    setmaxnreg_inc<224>();
     w_epilogue<MODE>(sm, tmem, g, sk, warp, lane);
     __syncwarp();
   }
