@@ -140,6 +140,30 @@ MOE_B200_API int moe_b200_route(const moe_b200_args* args, void* workspace, size
                    void* stream);
 
 /*
+ * Routing and permutation metadata with no workspace at all (no counterpart in the
+ * reference).  For callers that cannot allocate device memory when they call in: inference
+ * engines whose plugin/enqueue path forbids allocations because all device memory is planned
+ * up front, and latency-critical paths that cannot afford cudaMalloc's implicit device-wide
+ * synchronisation.  The scratch lives in a fixed 64 KB device array inside the library, so:
+ *   - num_tokens must be <= 256 (larger batches get MOE_B200_ERR_ARG; use moe_b200_route with
+ *     a workspace); num_local_experts <= 256;
+ *   - every call on a device shares that array: calls that overlap on the GPU (two streams or
+ *     two host threads on one device) race and must be serialised by the caller;
+ *   - the first call on a device looks up the array's device address (once per device).
+ * Only routing_logits, routing_bias, num_tokens, num_local_experts, local_expert_offset and
+ * routed_scaling_factor of `args` are read.  Outputs (device memory, caller-allocated):
+ *   topk_idx      int32 [T, 8]  selected global experts, ascending per token
+ *   topk_w        f32   [T, 8]  their combine weights
+ *   expert_count  int32 [E_local]  rows per local expert
+ *   row_token     int32 [T * min(8, E_local)]  token of each permuted row (expert-major)
+ *   row_weight    f32   [T * min(8, E_local)]  combine weight of each permuted row
+ * Results equal moe_b200_route's.  Nothing is allocated; no host synchronisation.
+ */
+MOE_B200_API int moe_b200_route_noalloc(const moe_b200_args* args, int32_t* topk_idx, float* topk_w,
+                                        int32_t* expert_count, int32_t* row_token, float* row_weight,
+                                        void* stream);
+
+/*
  * Synchronises the stream and returns the device status word (0 = ok,
  * otherwise the code of the first bounded wait that timed out); with
  * `clear` != 0 the word is reset.

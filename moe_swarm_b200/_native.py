@@ -33,6 +33,7 @@ EXPORTED = (
     "moe_b200_timer_destroy",
     "moe_b200_forward_timed",
     "moe_b200_timer_read",
+    "moe_b200_route_noalloc",
 )
 
 
@@ -98,6 +99,8 @@ def lib() -> ctypes.CDLL:
     l.moe_b200_forward_timed.restype = ctypes.c_int
     l.moe_b200_timer_read.argtypes = [vp, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_int32), i32]
     l.moe_b200_timer_read.restype = ctypes.c_int
+    l.moe_b200_route_noalloc.argtypes = [ctypes.POINTER(MoeArgs), vp, vp, vp, vp, vp, vp]
+    l.moe_b200_route_noalloc.restype = ctypes.c_int
     _lib = l
     return l
 

@@ -173,6 +173,8 @@ int launch_route(const moe_b200_args* a, uint8_t* ws, const moe::Layout& L, int 
 
 }  // namespace
 
+int moe::report_error(int code, const char* msg) { return fail(code, msg); }
+
 extern "C" {
 
 size_t moe_b200_workspace_size(int32_t num_tokens, int32_t num_local_experts) {

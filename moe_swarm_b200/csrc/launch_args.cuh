@@ -42,6 +42,9 @@ struct RouteArgs {
 };
 
 
+// Records `msg` as this thread's last error (moe_b200_last_error) and returns `code`.
+int report_error(int code, const char* msg);
+
 // Arguments of the grouped-GEMM kernels (streaming and wide variants, both modes).
 struct TileArgs {
   const Plan* plan;

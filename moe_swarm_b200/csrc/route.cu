@@ -20,6 +20,9 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <mutex>
+
+#include "../../include/moe_b200.h"
 #include "launch_args.cuh"
 #include "moe_internal.cuh"
 #include "ptx.cuh"
@@ -183,6 +186,7 @@ __device__ void scatter_token(const RouteArgs& a, int t, int tl, int lane,
                               const uint32_t (*s_mask)[kChunk / 32], const int* base) {
   const int k = __ldcg(a.tok_nloc + t);
   if (k == 0) {
+    if (a.out == nullptr) return;
     uint4* dst = reinterpret_cast<uint4*>(a.out + static_cast<size_t>(t) * kH);
     for (int j = lane; j < kH * 2 / 16; j += 32) dst[j] = make_uint4(0, 0, 0, 0);
     return;
@@ -202,6 +206,7 @@ __device__ void scatter_token(const RouteArgs& a, int t, int tl, int lane,
   int rows[kTopK];
 #pragma unroll
   for (int i = 0; i < kTopK; ++i) rows[i] = __shfl_sync(0xffffffffu, row, i);
+  if (a.a_perm == nullptr) return;   // routing metadata only
   // the 7 KB row moves in two halves of 7 independent 16-byte loads per lane (all loads
   // of a half issue before its stores)
   const uint4* src = reinterpret_cast<const uint4*>(a.hidden + static_cast<size_t>(t) * kH);
@@ -407,14 +412,13 @@ __global__ void __launch_bounds__(kRouteThreads) scatter_kernel(RouteArgs a) {
 constexpr int kRouteSmallT = 256;
 constexpr int kRouteSmallThreads = 1024;
 
-__global__ void __launch_bounds__(kRouteSmallThreads, 1) route_small_kernel(RouteArgs a) {
+__device__ __forceinline__ void route_small_body(const RouteArgs& a) {
   __shared__ float s_bias[kEG];
   __shared__ uint32_t s_mask[kEG][kChunk / 32];
   __shared__ int s_tmp[1024];
   __shared__ int s_start[kEG];
   __shared__ int s_base[kEG];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  pdl_launch_dependents();   // the GEMM that follows may run its prologue meanwhile
   for (int i = tid; i < kEG; i += blockDim.x) s_bias[i] = bf16_bits_to_float(a.bias[i]);
   __syncthreads();
   for (int t = warp; t < a.T; t += kRouteSmallThreads / 32) route_token(a, s_bias, t, lane);
@@ -427,6 +431,11 @@ __global__ void __launch_bounds__(kRouteSmallThreads, 1) route_small_kernel(Rout
     for (int tl = warp; tl < nt; tl += kRouteSmallThreads / 32) scatter_token(a, t0 + tl, tl, lane, s_mask, s_base);
     __syncthreads();
   }
+}
+
+__global__ void __launch_bounds__(kRouteSmallThreads, 1) route_small_kernel(RouteArgs a) {
+  pdl_launch_dependents();   // the GEMM that follows may run its prologue meanwhile
+  route_small_body(a);
 }
 
 cudaError_t route_launch(const RouteArgs& a, cudaStream_t st, int* launches) {
@@ -445,4 +454,131 @@ cudaError_t route_launch(const RouteArgs& a, cudaStream_t st, int* launches) {
   return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------------------
+// Routing without a caller-provided workspace (moe_b200_route_noalloc).
+//
+// Its scratch -- the per-token pick lists, chunk counts, segment tables and plan -- lives in
+// this file-scope array, sized for kNoAllocMaxT tokens and 256 local experts.  Every GPU that
+// loads the library holds these bytes until the process exits, and every call on a device
+// reuses the same bytes: calls that overlap on the GPU (two streams, or two host threads on
+// one device) race on them and must be serialised by the caller.
+constexpr int kNoAllocMaxT = 256;
+constexpr size_t kNoAllocScratchBytes = 64 * 1024;
+static __device__ __align__(256) unsigned char g_route_scratch[kNoAllocScratchBytes];
+
+struct NoAllocLayout {
+  size_t plan, chunk_hist, chunk_base, tok_le, tok_lw, tok_nloc, tok_rows, tables, total;
+};
+
+__host__ __device__ constexpr size_t na_align(size_t x) { return (x + 255) / 256 * 256; }
+
+__host__ __device__ constexpr NoAllocLayout noalloc_layout() {
+  NoAllocLayout l{};
+  l.plan = 0;
+  l.chunk_hist = na_align(l.plan + sizeof(Plan));
+  l.chunk_base = na_align(l.chunk_hist + 2 * kEG * sizeof(int));
+  l.tok_le = na_align(l.chunk_base + 2 * kEG * sizeof(int));
+  l.tok_lw = na_align(l.tok_le + kNoAllocMaxT * kTopK * sizeof(int));
+  l.tok_nloc = na_align(l.tok_lw + kNoAllocMaxT * kTopK * sizeof(float));
+  l.tok_rows = na_align(l.tok_nloc + kNoAllocMaxT * sizeof(int));
+  l.tables = na_align(l.tok_rows + kNoAllocMaxT * kTopK * sizeof(int));
+  l.total = na_align(l.tables + 6 * (kEG + 1) * sizeof(int));
+  return l;
+}
+static_assert(noalloc_layout().total <= kNoAllocScratchBytes, "no-alloc scratch too small");
+
+__global__ void __launch_bounds__(kRouteSmallThreads, 1) route_noalloc_kernel(RouteArgs a) {
+  // the chunk counts must start at zero; the array keeps the previous call's contents
+  for (int i = threadIdx.x; i < 2 * kEG; i += blockDim.x) a.chunk_hist[i] = 0;
+  __syncthreads();
+  route_small_body(a);
+}
+
 }  // namespace moe
+
+namespace {
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[256] = {};
+
+}  // namespace
+
+extern "C" MOE_B200_API int moe_b200_route_noalloc(const moe_b200_args* args, int32_t* topk_idx, float* topk_w,
+                                                  int32_t* expert_count, int32_t* row_token, float* row_weight,
+                                                  void* stream) {
+  using namespace moe;
+  if (!args) return report_error(MOE_B200_ERR_ARG, "null args");
+  const int T = args->num_tokens, E = args->num_local_experts;
+  if (T < 0 || E < 1 || E > kEG) return report_error(MOE_B200_ERR_ARG, "num_tokens < 0 or num_local_experts outside [1, 256]");
+  if (T > kNoAllocMaxT)
+    return report_error(MOE_B200_ERR_ARG,
+                        "moe_b200_route_noalloc: num_tokens exceeds the static scratch limit of 256 tokens "
+                        "(use moe_b200_route with a workspace)");
+  if (T == 0) return MOE_B200_OK;
+  if (!args->routing_logits || !args->routing_bias || !topk_idx || !topk_w || !expert_count || !row_token ||
+      !row_weight)
+    return report_error(MOE_B200_ERR_ARG, "null tensor pointer");
+  if ((reinterpret_cast<uintptr_t>(args->routing_logits) & 15u) != 0)
+    return report_error(MOE_B200_ERR_ARG, "routing_logits must be 16-byte aligned");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return report_error(MOE_B200_ERR_CUDA, cudaGetErrorString(e));
+  if (dev < 0 || dev >= 256) return report_error(MOE_B200_ERR_DEVICE, "device index out of range");
+  int major = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  if (major != 10) return report_error(MOE_B200_ERR_DEVICE, "an sm_100 (B200-class) device is required");
+  void* scratch = nullptr;
+  {
+    // one-time set-up per device (with that device current): the device address of the array.
+    // The array's name in host code is only a host-side handle, never a device address.
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+      void* p = nullptr;
+      e = cudaGetSymbolAddress(&p, g_route_scratch);
+      if (e != cudaSuccess) return report_error(MOE_B200_ERR_CUDA, cudaGetErrorString(e));
+      g_noalloc_ptr[dev] = p;
+    }
+    scratch = g_noalloc_ptr[dev];
+  }
+  constexpr NoAllocLayout L = noalloc_layout();
+  uint8_t* sp = static_cast<uint8_t*>(scratch);
+  RouteArgs r{};
+  r.logits = args->routing_logits;
+  r.bias = args->routing_bias;
+  r.T = T;
+  r.E = E;
+  r.offset = args->local_expert_offset;
+  r.rsf = args->routed_scaling_factor;
+  r.nchunks = (T + kChunk - 1) / kChunk;
+  r.num_sms = 148;
+  r.r_pad = 0;
+  r.plan = reinterpret_cast<Plan*>(sp + L.plan);
+  r.topk_idx = topk_idx;
+  r.topk_w = topk_w;
+  r.tok_nloc = reinterpret_cast<int*>(sp + L.tok_nloc);
+  r.tok_le = reinterpret_cast<int*>(sp + L.tok_le);
+  r.tok_lw = reinterpret_cast<float*>(sp + L.tok_lw);
+  r.tok_rows = reinterpret_cast<int*>(sp + L.tok_rows);
+  r.chunk_hist = reinterpret_cast<int*>(sp + L.chunk_hist);
+  r.chunk_base = reinterpret_cast<int*>(sp + L.chunk_base);
+  int* tab = reinterpret_cast<int*>(sp + L.tables);
+  r.e_count = expert_count;
+  r.e_start = tab;
+  r.e_mt_start = tab + (kEG + 1);
+  r.e_u1 = tab + 2 * (kEG + 1);
+  r.e_u2 = tab + 3 * (kEG + 1);
+  r.e_tt = tab + 4 * (kEG + 1);
+  r.e_m64 = tab + 5 * (kEG + 1);
+  r.row_token = row_token;
+  r.row_weight = row_weight;
+  // no activation copy and no output rows: routing and permutation metadata only
+  r.hidden = nullptr;
+  r.hs_scale = nullptr;
+  r.out = nullptr;
+  r.a_perm = nullptr;
+  r.sa_perm = nullptr;
+  route_noalloc_kernel<<<1, kRouteSmallThreads, 0, static_cast<cudaStream_t>(stream)>>>(r);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return report_error(MOE_B200_ERR_CUDA, cudaGetErrorString(e));
+  return MOE_B200_OK;
+}
