@@ -74,6 +74,9 @@ struct WideSmem {
   int flag;
   float ssw[2][kKB1];      // this segment's weight scales (MODE 1: X1, X2 blocks)
   float amx[2][128];       // MODE 1: per-row amax of each column half
+  // per-epilogue-warp staging of output rows so each warp store writes whole row segments
+  alignas(16) uint8_t ostg[8][2560];
+  int mt[8][16];           // MODE 2: per-warp row metadata (token, local expert count)
   int e_cnt[kEG + 1];
   int e_start[kEG + 1];
   int e_tiles[kEG + 1];
@@ -242,7 +245,7 @@ done:
 // MODE 1 tile epilogue: SwiGLU of this thread's 64 (X1, X2) column pairs of row `rit`, the row's
 // 128-column amax (exchanged with the other column half), hi/lo e4m3 encoding and stores.
 __device__ __forceinline__ void w_epi1(WideSmem& sm, const TileArgs& g, const WTile& s, float* x1,
-                                       const float* x2, int h, int rit) {
+                                       const float* x2, int h, int rit, uint32_t* hw, uint32_t* lw) {
   float amax = 0.f;
 #pragma unroll
   for (int j = 0; j < 64; ++j) {
@@ -252,10 +255,7 @@ __device__ __forceinline__ void w_epi1(WideSmem& sm, const TileArgs& g, const WT
   sm.amx[h][rit] = amax;
   named_bar_sync(1, kWEpiThreads);
   amax = fmaxf(sm.amx[0][rit], sm.amx[1][rit]);
-  if (rit >= s.nr) return;
-  const size_t row = static_cast<size_t>(s.row0 + rit);
   const float inv = amax > 0.f ? 448.0f / amax : 0.f;
-  uint32_t hw[16], lw[16];
 #pragma unroll
   for (int j = 0; j < 64; j += 4) {
     const float y0 = x1[j] * inv, y1 = x1[j + 1] * inv, y2 = x1[j + 2] * inv, y3 = x1[j + 3] * inv;
@@ -267,44 +267,72 @@ __device__ __forceinline__ void w_epi1(WideSmem& sm, const TileArgs& g, const WT
     hw[j / 4] = h01 | (h23 << 16);
     lw[j / 4] = l01 | (l23 << 16);
   }
-  const size_t off = row * kI + static_cast<size_t>(s.nt) * kBlk + 64 * h;
-  uint4* dh = reinterpret_cast<uint4*>(g.c_hi + off);
-  uint4* dl = reinterpret_cast<uint4*>(g.c_lo + off);
+  if (h == 0 && rit < s.nr)
+    g.c_scale[static_cast<size_t>(s.nt) * g.r_pad + s.row0 + rit] = amax > 0.f ? amax / 448.0f : 1.0f;
+}
+
+// Stores this warp's 32 rows x 64 bytes (hi, then lo) through its staging buffer: each lane
+// stages its row, then every warp store writes 8 whole 64-byte row segments.
+__device__ __forceinline__ void w_store1(WideSmem& sm, const TileArgs& g, const WTile& s, const uint32_t* hw,
+                                         const uint32_t* lw, int ew, int q, int h, int lane) {
+  uint8_t* st = sm.ostg[ew];
+  const int rows_here = min(32, s.nr - 32 * q);   // valid rows of this warp's quarter
 #pragma unroll
-  for (int v = 0; v < 4; ++v) {
-    dh[v] = make_uint4(hw[4 * v], hw[4 * v + 1], hw[4 * v + 2], hw[4 * v + 3]);
-    dl[v] = make_uint4(lw[4 * v], lw[4 * v + 1], lw[4 * v + 2], lw[4 * v + 3]);
+  for (int part = 0; part < 2; ++part) {
+    const uint32_t* src = part == 0 ? hw : lw;
+    uint4* mine = reinterpret_cast<uint4*>(st + lane * 80);
+#pragma unroll
+    for (int v = 0; v < 4; ++v) mine[v] = make_uint4(src[4 * v], src[4 * v + 1], src[4 * v + 2], src[4 * v + 3]);
+    __syncwarp();
+    uint8_t* base = (part == 0 ? g.c_hi : g.c_lo) + static_cast<size_t>(s.row0 + 32 * q) * kI +
+                    static_cast<size_t>(s.nt) * kBlk + 64 * h;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = 8 * i + (lane >> 2), ch = lane & 3;
+      if (r < rows_here)
+        *reinterpret_cast<uint4*>(base + static_cast<size_t>(r) * kI + 16 * ch) =
+            *reinterpret_cast<const uint4*>(st + r * 80 + 16 * ch);
+    }
+    __syncwarp();
   }
-  if (h == 0) g.c_scale[static_cast<size_t>(s.nt) * g.r_pad + row] = amax > 0.f ? amax / 448.0f : 1.0f;
 }
 
 // MODE 2 tile epilogue: hi + lo, then this thread's 128 output columns of token `tok` (lanes
 // 0..15 of each quarter): the bf16 output row directly for a token with one local expert,
 // otherwise the routing-weighted fp32 row for the combine kernel.
-__device__ __forceinline__ void w_epi2(const TileArgs& g, const WTile& s, float* acc, int h, int q, int lane) {
+__device__ __forceinline__ void w_epi2(WideSmem& sm, const TileArgs& g, const WTile& s, float* acc, int ew, int h,
+                                       int q, int lane, int t, float w, int kt) {
 #pragma unroll
   for (int j = 0; j < 128; ++j) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], 16);
-  const int tok = 16 * q + (lane & 15);
-  if (lane >= 16 || tok >= s.nr) return;
-  const int row = s.row0 + tok;
-  const int t = __ldg(g.row_token + row);
-  const float w = __ldg(g.row_weight + row);
-  const int kt = __ldg(g.tok_nloc + t);
+  // lanes 0..15 own token rows 16q + lane; each warp writes its 16 rows x 128 columns in four
+  // rounds of 32 columns staged through shared memory, 4 whole 128-byte row segments per store
+  const int rows_here = min(16, s.nr - 16 * q);
+  float* st = reinterpret_cast<float*>(sm.ostg[ew]);   // [16][36]
+  if (lane < 16) sm.mt[ew][lane] = kt == 1 ? -1 - t : t;   // < 0: the bf16 output row of token -1-v
   const int col0 = s.nt * 256 + 128 * h;
-  if (kt == 1) {
-    uint4* o = reinterpret_cast<uint4*>(g.out + static_cast<size_t>(t) * kH + col0);
 #pragma unroll
-    for (int v = 0; v < 16; ++v)
-      o[v] = make_uint4(bf16x2_bits(__fmul_rn(acc[8 * v], w), __fmul_rn(acc[8 * v + 1], w)),
-                        bf16x2_bits(__fmul_rn(acc[8 * v + 2], w), __fmul_rn(acc[8 * v + 3], w)),
-                        bf16x2_bits(__fmul_rn(acc[8 * v + 4], w), __fmul_rn(acc[8 * v + 5], w)),
-                        bf16x2_bits(__fmul_rn(acc[8 * v + 6], w), __fmul_rn(acc[8 * v + 7], w)));
-  } else {
-    float4* p = reinterpret_cast<float4*>(g.part2 + static_cast<size_t>(row) * kH + col0);
+  for (int rd = 0; rd < 4; ++rd) {
+    if (lane < 16) {
 #pragma unroll
-    for (int v = 0; v < 32; ++v)
-      p[v] = make_float4(__fmul_rn(acc[4 * v], w), __fmul_rn(acc[4 * v + 1], w), __fmul_rn(acc[4 * v + 2], w),
-                         __fmul_rn(acc[4 * v + 3], w));
+      for (int j = 0; j < 32; ++j) st[lane * 36 + j] = __fmul_rn(acc[32 * rd + j], w);
+    }
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = 4 * i + (lane >> 3), ch = lane & 7;
+      if (r < rows_here) {
+        const float4 v = *reinterpret_cast<const float4*>(st + r * 36 + 4 * ch);
+        const int tv = sm.mt[ew][r];
+        const int col = col0 + 32 * rd + 4 * ch;
+        if (tv < 0) {
+          *reinterpret_cast<uint2*>(g.out + static_cast<size_t>(-1 - tv) * kH + col) =
+              make_uint2(bf16x2_bits(v.x, v.y), bf16x2_bits(v.z, v.w));
+        } else {
+          *reinterpret_cast<float4*>(g.part2 + static_cast<size_t>(s.row0 + 16 * q + r) * kH + col) = v;
+        }
+      }
+    }
+    __syncwarp();
   }
 }
 
@@ -329,6 +357,16 @@ __device__ __forceinline__ void w_epilogue(WideSmem& sm, uint32_t tmem, const Ti
     const int trow = MODE == 1 ? rit : 16 * q + (lane & 15);
     const size_t srow = static_cast<size_t>(s.row0 + min(trow, s.nr - 1));
     const float lo_scale = (MODE == 2 && lane >= 16) ? 0.0625f : 1.0f;
+    // a lane quarter holding only padding rows skips its TMEM loads and FMAs
+    const bool qlive = (MODE == 1 ? 32 * q : 16 * q) < s.nr;
+    // MODE 2: the token metadata of this thread's row, fetched while the K loop runs
+    int meta_t = 0, meta_k = 0;
+    float meta_w = 0.f;
+    const bool meta_mine = MODE == 2 && lane < 16 && trow < s.nr;
+    if (meta_mine) {
+      meta_t = __ldg(g.row_token + s.row0 + trow);
+      meta_w = __ldg(g.row_weight + s.row0 + trow);
+    }
     const float* swp1;
     const float* swp2;
     if (MODE == 1) {
@@ -367,7 +405,12 @@ __device__ __forceinline__ void w_epilogue(WideSmem& sm, uint32_t tmem, const Ti
         dead = true;
       MOE_WADD(tw, t0);
       t0 = MOE_WCLK();
-      if (!dead) {
+      if (!dead && !qlive) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.tempty[buf]);
+      }
+      if (!dead && qlive) {
         tc_fence_after();
         const uint32_t base = lane_base + buf * 256u;
         if (MODE == 1) {
@@ -421,6 +464,7 @@ __device__ __forceinline__ void w_epilogue(WideSmem& sm, uint32_t tmem, const Ti
         }
       }
       MOE_WADD(tp, t0);
+      if (MODE == 2 && ki == 0 && meta_mine) meta_k = __ldg(g.tok_nloc + meta_t);   // t arrived by now
       tk ^= 1u << buf;
       buf ^= 1u;
     }
@@ -476,10 +520,13 @@ __device__ __forceinline__ void w_epilogue(WideSmem& sm, uint32_t tmem, const Ti
     MOE_WADD(tf, t0);
     t0 = MOE_WCLK();
     // (after an abort the epilogue still runs, on garbage, so every warp meets every barrier)
-    if (MODE == 1)
-      w_epi1(sm, g, s, acc1, acc2, h, rit);
+    if (MODE == 1) {
+      uint32_t hw[16], lw[16];
+      w_epi1(sm, g, s, acc1, acc2, h, rit, hw, lw);
+      w_store1(sm, g, s, hw, lw, ew, q, h, lane);
+    }
     else
-      w_epi2(g, s, acc1, h, q, lane);
+      w_epi2(sm, g, s, acc1, ew, h, q, lane, meta_t, meta_w, meta_k);
     MOE_WADD(te, t0);
   }
 #ifdef MOE_TRACE
