@@ -45,6 +45,7 @@ S13_BYTES = 32 * 56 * 4
 S2_BYTES = 56 * 16 * 4
 FLOP_PER_ASSIGN = 2 * (H * 2 * I) + 2 * (I * H)   # 88,080,384 (GEMM1 + GEMM2)
 EP_T = 4096
+STREAM_MAX_T = 512             # T at or below which the layer runs the swap-AB streaming kernels
 
 
 def peaks():
@@ -269,6 +270,25 @@ def sweep(device, steps, peaks_):
 
 
 # ----------------------------------------------------------------------------- main
+def profile_case(args):
+    """A small fixed workload for ncu captures: the same layer calls as the bench, no timing."""
+    import moe_swarm_b200 as M
+    import moe_swarm_b200.workload as W
+    T, E = (int(v) for v in args.case.split(":"))
+    dev = torch.device("cuda", 0)
+    x = {k: v.to(dev) for k, v in W.make_activations(T, 5).items()}
+    x.update(W.make_weights_fast(E, 1, device=dev))
+    x["local_expert_offset"] = 0
+    x["routed_scaling_factor"] = 2.5
+    for _ in range(args.warmup + args.steps):
+        M.run(**x)
+    torch.cuda.synchronize()
+    status = M.device_status(dev)
+    print(f"case T={T} E={E}: {args.warmup + args.steps} calls, device status {status}", flush=True)
+    if status != 0:
+        raise SystemExit(1)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -277,7 +297,12 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-sweeps", action="store_true")
     ap.add_argument("--cpu-experts", type=int, default=8)
+    ap.add_argument("--case", default=None, metavar="T:E",
+                    help="profiling case: W + K untimed layer calls at T tokens with E local experts "
+                         "(seeded inputs, weights generated on the device); prints a status line only")
     args = ap.parse_args()
+    if args.case:
+        return profile_case(args)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
@@ -443,7 +468,8 @@ def main():
         "latency_us": round(ms_per_step * 1e3, 1),
         "stage_us": {k: round(v * 1e3, 1) for k, v in zip(("route", "gemm1", "gemm2"), per_launch_ms)},
         "routing": {"active_experts_rank0": f["active"], "rows_rank0": f["rows"]},
-        "roofline": {"kernel": f"gemm_kernel<{dom}>", "bound": "hbm", "achieved": round(achieved, 1),
+        "roofline": {"kernel": f"{'stream' if T <= STREAM_MAX_T else 'wide'}_kernel<{dom}>", "bound": "hbm",
+                     "achieved": round(achieved, 1),
                      "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 3),
                      "traffic": traffic, "algorithmic_bytes_per_launch": dom_bytes,
                      "peak_source": pk["source"] + " (MEASURED_PEAKS.json hbm_gbs, burst copy)"},

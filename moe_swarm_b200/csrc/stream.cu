@@ -127,9 +127,11 @@ __device__ __forceinline__ uint16_t bf16_bits(float v) {
   return *reinterpret_cast<uint16_t*>(&b);
 }
 
+// The whole producer warp runs this loop; lane j issues box j of a stage, so a stage's boxes
+// do not queue behind one another in the TMA unit as they do when one thread issues them all.
 template <int MODE>
 __device__ void s_producer(StreamSmem<MODE>& sm, const CUtensorMap* tmW, const CUtensorMap* tmT,
-                           const CUtensorMap* tmT2, const TileArgs& g, const Sched& sk) {
+                           const CUtensorMap* tmT2, const TileArgs& g, const Sched& sk, int lane) {
   constexpr int ST = SCfg<MODE>::STAGES;
   uint32_t stage = 0, phase = 0, issued = 0, lastpar = 0;
   long long tw = 0, nkb = 0;
@@ -145,24 +147,25 @@ __device__ void s_producer(StreamSmem<MODE>& sm, const CUtensorMap* tmW, const C
     const STile s = s_decode<MODE>(sm, g.E, tile);
     for (int kb = k0; kb < k1; ++kb) {
       const long long t0 = MOE_TCLK();
-      if (!mbar_wait(&sm.empty[stage], phase ^ 1u, &sm.abort, g.status, kStWaitProducer)) goto drain;
+      const bool ok = mbar_wait(&sm.empty[stage], phase ^ 1u, &sm.abort, g.status, kStWaitProducer);
+      if (!__all_sync(0xffffffffu, ok)) goto drain;
       MOE_TADD(tw, t0);
       ++nkb;
-      mbar_arrive_expect_tx(&sm.full[stage], SCfg<MODE>::STAGE_BYTES);
+      if (lane == 0) mbar_arrive_expect_tx(&sm.full[stage], SCfg<MODE>::STAGE_BYTES);
+      __syncwarp();
       uint8_t* st = sm.stage[stage];
       if (MODE == 1) {
-        tma_load_2d(st, tmW, &sm.full[stage], kb * kBlk, s.e * kN1 + s.nt * kBlk);
-        tma_load_2d(st + 16384, tmW, &sm.full[stage], kb * kBlk, s.e * kN1 + kI + s.nt * kBlk);
-        tma_load_2d(st + 32768, tmT, &sm.full[stage], kb * kBlk, s.row0);
+        if (lane == 0) tma_load_2d(st, tmW, &sm.full[stage], kb * kBlk, s.e * kN1 + s.nt * kBlk);
+        if (lane == 1) tma_load_2d(st + 16384, tmW, &sm.full[stage], kb * kBlk, s.e * kN1 + kI + s.nt * kBlk);
+        if (lane == 2) tma_load_2d(st + 32768, tmT, &sm.full[stage], kb * kBlk, s.row0);
       } else {
-        tma_load_2d(st, tmW, &sm.full[stage], kb * kBlk, s.e * kH + s.nt * kBlk);
+        if (lane == 2) tma_load_2d(st, tmW, &sm.full[stage], kb * kBlk, s.e * kH + s.nt * kBlk);
         if (!waited) {
           pend_row0[pend_n] = s.row0;
           pend_kb[pend_n] = kb;
           ++pend_n;
-        } else {
-          tma_load_2d(st + 16384, tmT, &sm.full[stage], kb * kBlk, s.row0);
-          tma_load_2d(st + 16384 + kTok * 128, tmT2, &sm.full[stage], kb * kBlk, s.row0);
+        } else if (lane < 2) {
+          tma_load_2d(st + 16384 + lane * (kTok * 128), lane ? tmT2 : tmT, &sm.full[stage], kb * kBlk, s.row0);
         }
       }
       issued |= 1u << stage;
@@ -174,32 +177,34 @@ __device__ void s_producer(StreamSmem<MODE>& sm, const CUtensorMap* tmW, const C
       if (MODE == 2 && !waited && pend_n == ST) {
         pdl_wait();
         waited = true;
-        for (int i = 0; i < pend_n; ++i) {
-          uint8_t* sp = sm.stage[i];
-          tma_load_2d(sp + 16384, tmT, &sm.full[i], pend_kb[i] * kBlk, pend_row0[i]);
-          tma_load_2d(sp + 16384 + kTok * 128, tmT2, &sm.full[i], pend_kb[i] * kBlk, pend_row0[i]);
-        }
+        for (int i = 0; i < pend_n; ++i)
+          if (lane < 2)
+            tma_load_2d(sm.stage[i] + 16384 + lane * (kTok * 128), lane ? tmT2 : tmT, &sm.full[i], pend_kb[i] * kBlk,
+                        pend_row0[i]);
         pend_n = 0;
       }
     }
   }
   if (MODE == 2 && !waited) {   // fewer K-blocks than stages
     pdl_wait();
-    for (int i = 0; i < pend_n; ++i) {
-      uint8_t* sp = sm.stage[i];
-      tma_load_2d(sp + 16384, tmT, &sm.full[i], pend_kb[i] * kBlk, pend_row0[i]);
-      tma_load_2d(sp + 16384 + kTok * 128, tmT2, &sm.full[i], pend_kb[i] * kBlk, pend_row0[i]);
-    }
+    for (int i = 0; i < pend_n; ++i)
+      if (lane < 2)
+        tma_load_2d(sm.stage[i] + 16384 + lane * (kTok * 128), lane ? tmT2 : tmT, &sm.full[i], pend_kb[i] * kBlk,
+                    pend_row0[i]);
   }
 drain:
-  for (int s = 0; s < ST; ++s)
-    if ((issued >> s) & 1u) {
-      int no_abort = 0;
-      mbar_wait(&sm.full[s], (lastpar >> s) & 1u, &no_abort, g.status, kStWaitDrain);
-    }
+  if (lane == 0)
+    for (int s = 0; s < ST; ++s)
+      if ((issued >> s) & 1u) {
+        int no_abort = 0;
+        mbar_wait(&sm.full[s], (lastpar >> s) & 1u, &no_abort, g.status, kStWaitDrain);
+      }
+  __syncwarp();
 #ifdef MOE_TRACE
-  g.trace[blockIdx.x * kTraceSlots + 2] = tw;
-  g.trace[blockIdx.x * kTraceSlots + 3] = nkb;
+  if (lane == 0) {
+    g.trace[blockIdx.x * kTraceSlots + 2] = tw;
+    g.trace[blockIdx.x * kTraceSlots + 3] = nkb;
+  }
 #endif
 }
 
@@ -526,8 +531,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
 #endif
   const uint32_t tmem = sm.tmem_base;
   if (warp == 0) {
-    if (lane == 0) s_producer<MODE>(sm, &tmW, &tmT, &tmT2, g, sk);
-    __syncwarp();
+    s_producer<MODE>(sm, &tmW, &tmT, &tmT2, g, sk, lane);
   } else if (warp == 1) {
     if (lane == 0) s_mma<MODE>(sm, tmem, g, sk);
     __syncwarp();

@@ -17,9 +17,9 @@
 //     expert gets its bf16 output row directly, otherwise w * O goes to its fp32 partial row,
 //     summed in ascending expert order by the combine kernel (combine.cu).
 //
-// CTA = 12 warps: warp 0 TMA producer, warp 1 TMEM owner + single-thread MMA issuer (their
-// warpgroup drops to 40 registers), warps 4..11 promotion/epilogue with 232 registers: two
-// warps per TMEM lane quarter, one per column half.
+// CTA = 12 warps: warp 0 TMA producer (one box per lane), warp 1 TMEM owner + single-thread MMA
+// issuer (their warpgroup drops to 56 registers), warps 4..11 promotion/epilogue with 224
+// registers: two warps per TMEM lane quarter, one per column half.
 // 4 smem stages of 48 KB, 2 TMEM accumulator buffers of 256 columns.  Work: data-parallel
 // whole tiles, then a stream-K tail (sched.cuh).  No TMA multicast (the kernels also run in the
 // multi-GPU expert-parallel configuration).
@@ -114,9 +114,19 @@ __device__ __forceinline__ uint32_t bf16x2_bits(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&b);
 }
 
+// One box of a MODE 2 token tile: box j < 8 is hi (even j) or lo (odd j) of row group j / 2.
+__device__ __forceinline__ void w_load_c(uint8_t* st, const CUtensorMap* tmA, const CUtensorMap* tmA2, uint64_t* bar,
+                                         int kb, int row0, int j) {
+  const int q = j >> 1;
+  tma_load_2d(st + q * 4096 + (j & 1) * 2048, (j & 1) ? tmA2 : tmA, bar, kb * kBlk, row0 + 16 * q);
+}
+
+// The whole producer warp runs this loop; each lane issues at most one box of a stage.  Tiled
+// loads issued by one thread go through the TMA unit one after another (about 330 cycles per
+// 16 KB box); issued by several lanes of a warp they overlap.
 template <int MODE>
 __device__ __forceinline__ void w_producer(WideSmem& sm, const CUtensorMap* tmA, const CUtensorMap* tmA2,
-                           const CUtensorMap* tmB, const TileArgs& g, const Sched& sk) {
+                           const CUtensorMap* tmB, const TileArgs& g, const Sched& sk, int lane) {
   uint32_t stage = 0, phase = 0, issued = 0, lastpar = 0;
   long long tw = 0, nkb = 0;
   // MODE 2: the first stages get their weight tiles before the dependency on GEMM1 resolves
@@ -130,28 +140,27 @@ __device__ __forceinline__ void w_producer(WideSmem& sm, const CUtensorMap* tmA,
     const WTile s = w_decode<MODE>(sm, g.E, tile);
     for (int kb = k0; kb < k1; ++kb) {
       const long long t0 = MOE_WCLK();
-      if (!mbar_wait(&sm.empty[stage], phase ^ 1u, &sm.abort, g.status, kStWaitProducer)) goto drain;
+      const bool ok = mbar_wait(&sm.empty[stage], phase ^ 1u, &sm.abort, g.status, kStWaitProducer);
+      if (!__all_sync(0xffffffffu, ok)) goto drain;
       MOE_WADD(tw, t0);
       ++nkb;
-      mbar_arrive_expect_tx(&sm.full[stage], kWStageBytes);
+      // the stage's byte count is armed before any lane's copy can complete it
+      if (lane == 0) mbar_arrive_expect_tx(&sm.full[stage], kWStageBytes);
+      __syncwarp();
       uint8_t* st = sm.stage[stage];
       if (MODE == 1) {
-        tma_load_2d(st, tmA, &sm.full[stage], kb * kBlk, s.row0);
-        tma_load_2d(st + 16384, tmB, &sm.full[stage], kb * kBlk, s.e * kN1 + s.nt * kBlk);
-        tma_load_2d(st + 32768, tmB, &sm.full[stage], kb * kBlk, s.e * kN1 + kI + s.nt * kBlk);
+        if (lane == 0) tma_load_2d(st, tmA, &sm.full[stage], kb * kBlk, s.row0);
+        if (lane == 1) tma_load_2d(st + 16384, tmB, &sm.full[stage], kb * kBlk, s.e * kN1 + s.nt * kBlk);
+        if (lane == 2) tma_load_2d(st + 32768, tmB, &sm.full[stage], kb * kBlk, s.e * kN1 + kI + s.nt * kBlk);
       } else {
-        tma_load_2d(st + 16384, tmB, &sm.full[stage], kb * kBlk, s.e * kH + s.nt * 256);
-        tma_load_2d(st + 32768, tmB, &sm.full[stage], kb * kBlk, s.e * kH + s.nt * 256 + 128);
+        if (lane == 8) tma_load_2d(st + 16384, tmB, &sm.full[stage], kb * kBlk, s.e * kH + s.nt * 256);
+        if (lane == 9) tma_load_2d(st + 32768, tmB, &sm.full[stage], kb * kBlk, s.e * kH + s.nt * 256 + 128);
         if (!waited) {
           pend_row0[pend_n] = s.row0;
           pend_kb[pend_n] = kb;
           ++pend_n;
-        } else {
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            tma_load_2d(st + q * 4096, tmA, &sm.full[stage], kb * kBlk, s.row0 + 16 * q);
-            tma_load_2d(st + q * 4096 + 2048, tmA2, &sm.full[stage], kb * kBlk, s.row0 + 16 * q);
-          }
+        } else if (lane < 8) {
+          w_load_c(st, tmA, tmA2, &sm.full[stage], kb, s.row0, lane);
         }
       }
       issued |= 1u << stage;
@@ -164,12 +173,7 @@ __device__ __forceinline__ void w_producer(WideSmem& sm, const CUtensorMap* tmA,
         pdl_wait();
         waited = true;
         for (int i = 0; i < pend_n; ++i)
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            tma_load_2d(sm.stage[i] + q * 4096, tmA, &sm.full[i], pend_kb[i] * kBlk, pend_row0[i] + 16 * q);
-            tma_load_2d(sm.stage[i] + q * 4096 + 2048, tmA2, &sm.full[i], pend_kb[i] * kBlk,
-                        pend_row0[i] + 16 * q);
-          }
+          if (lane < 8) w_load_c(sm.stage[i], tmA, tmA2, &sm.full[i], pend_kb[i], pend_row0[i], lane);
         pend_n = 0;
       }
     }
@@ -177,21 +181,21 @@ __device__ __forceinline__ void w_producer(WideSmem& sm, const CUtensorMap* tmA,
   if (MODE == 2 && !waited) {
     pdl_wait();
     for (int i = 0; i < pend_n; ++i)
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        tma_load_2d(sm.stage[i] + q * 4096, tmA, &sm.full[i], pend_kb[i] * kBlk, pend_row0[i] + 16 * q);
-        tma_load_2d(sm.stage[i] + q * 4096 + 2048, tmA2, &sm.full[i], pend_kb[i] * kBlk, pend_row0[i] + 16 * q);
-      }
+      if (lane < 8) w_load_c(sm.stage[i], tmA, tmA2, &sm.full[i], pend_kb[i], pend_row0[i], lane);
   }
 drain:
-  for (int s = 0; s < kWStages; ++s)
-    if ((issued >> s) & 1u) {
-      int no_abort = 0;
-      mbar_wait(&sm.full[s], (lastpar >> s) & 1u, &no_abort, g.status, kStWaitDrain);
-    }
+  if (lane == 0)
+    for (int s = 0; s < kWStages; ++s)
+      if ((issued >> s) & 1u) {
+        int no_abort = 0;
+        mbar_wait(&sm.full[s], (lastpar >> s) & 1u, &no_abort, g.status, kStWaitDrain);
+      }
+  __syncwarp();
 #ifdef MOE_TRACE
-  g.trace[blockIdx.x * kTraceSlots + 2] = tw;
-  g.trace[blockIdx.x * kTraceSlots + 3] = nkb;
+  if (lane == 0) {
+    g.trace[blockIdx.x * kTraceSlots + 2] = tw;
+    g.trace[blockIdx.x * kTraceSlots + 3] = nkb;
+  }
 #endif
 }
 
@@ -594,8 +598,7 @@ __global__ void __launch_bounds__(kWThreads, 1)
   if (warp < 4) {
     setmaxnreg_dec<56>();
     if (warp == 0) {
-      if (lane == 0) w_producer<MODE>(sm, &tmA, &tmA2, &tmB, g, sk);
-      __syncwarp();
+      w_producer<MODE>(sm, &tmA, &tmA2, &tmB, g, sk, lane);
     } else if (warp == 1) {
       if (lane == 0) w_mma(sm, tmem, g, sk);
       __syncwarp();
