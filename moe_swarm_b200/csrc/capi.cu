@@ -163,9 +163,13 @@ int prepare(const moe_b200_args* a, void* workspace, size_t ws_bytes, moe::Layou
   return MOE_B200_OK;
 }
 
+// zero_rows: the routing kernels also write the zero output rows of tokens with no local
+// expert (moe_b200_route); the full layer leaves them to the combine kernel instead, which
+// runs on every SM rather than on the single routing CTA of small batches.
 int launch_route(const moe_b200_args* a, uint8_t* ws, const moe::Layout& L, int sms, cudaStream_t st,
-                 int* launches) {
+                 int* launches, bool zero_rows) {
   moe::RouteArgs r = make_route_args(a, ws, L, sms);
+  if (!zero_rows) r.out = nullptr;
   cudaError_t e = moe::route_launch(r, st, launches);
   if (e != cudaSuccess) return cuda_fail(e, "route launch");
   return MOE_B200_OK;
@@ -225,7 +229,7 @@ int moe_b200_route(const moe_b200_args* a, void* workspace, size_t ws_bytes, voi
   if (a->num_tokens == 0) return MOE_B200_OK;
   int launches = 0;
   return launch_route(a, static_cast<uint8_t*>(workspace), L, device_info(dev).sms,
-                      static_cast<cudaStream_t>(stream), &launches);
+                      static_cast<cudaStream_t>(stream), &launches, true);
 }
 
 }  // extern "C"
@@ -308,7 +312,7 @@ int forward_impl(const moe_b200_args* a, void* workspace, size_t ws_bytes, void*
     cudaEventRecord(ev[0], st);
   }
   int launches = 0;
-  rc = launch_route(a, ws, L, di.sms, st, &launches);
+  rc = launch_route(a, ws, L, di.sms, st, &launches, false);
   if (rc) return rc;
   if (ev) cudaEventRecord(ev[1], st);
 

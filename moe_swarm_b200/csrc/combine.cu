@@ -3,7 +3,7 @@
 // where the GEMM2 kernels left each w_e * O_e row in fp32 in the partial-row buffer.  This is
 // the accumulation order of the reference's per-expert index_add_
 // (spec/reference_official.py:134-166), so the result is deterministic.  Tokens with one local
-// expert were written by GEMM2 directly and tokens with none by the routing kernel.
+// expert were written by GEMM2 directly; tokens with none get their zero row here.
 #include <cuda_bf16.h>
 
 #include "launch_args.cuh"
@@ -19,7 +19,12 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const int* tok
   pdl_wait();   // the partial rows come from GEMM2
   for (int t = blockIdx.x; t < T; t += gridDim.x) {
     const int kt = __ldg(tok_nloc + t);
-    if (kt <= 1) continue;
+    if (kt == 1) continue;
+    if (kt == 0) {
+      uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(t) * kH);
+      for (int v = threadIdx.x; v < kH * 2 / 16; v += kCombineThreads) dst[v] = make_uint4(0, 0, 0, 0);
+      continue;
+    }
     int rows[kTopK];
 #pragma unroll
     for (int a = 0; a < kTopK; ++a) rows[a] = a < kt ? __ldg(tok_rows + static_cast<size_t>(t) * kTopK + a) : 0;
