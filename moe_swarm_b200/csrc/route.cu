@@ -14,9 +14,9 @@
 // own group g), 8 tokens per CTA.  Local picks are counted per 128-token chunk with global
 // atomics (order-independent sums).  The last CTA to finish (a self-resetting arrival
 // counter) turns the chunk counts into expert segment starts, per-chunk bases and the GEMM
-// tile tables (plan), zeroes the counts for the next call, and, when T <= 128, performs the
-// permutation itself.  scatter_kernel (T > 128): 8 tokens per CTA; the rank of a token in an
-// expert's segment is a popcount over the chunk's per-expert token bitmask plus the chunk base.
+// tile tables (plan) and zeroes the counts for the next call.  scatter_kernel: 8 tokens per
+// CTA; the rank of a token in an expert's segment is a popcount over the chunk's per-expert
+// token bitmask plus the chunk base.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -127,26 +127,33 @@ __device__ void route_token(const RouteArgs& a, const float* s_bias, int t, int 
     rank += (o > gscore || (o == gscore && h < g)) ? 1 : 0;
   }
   const bool keep = rank < kTopKGroup;
-  // top-8 among the kept groups: 8 rounds of a warp-wide argmax (ties -> lower expert id)
+  // top-8 among the kept groups: 8 rounds of a warp-wide argmax (ties -> lower expert id).
+  // Each lane keeps the key of its best remaining expert; a round is one warp max (redux) and
+  // a ballot for the lowest lane holding it, and only the winning lane rescans its slots.
   uint32_t taken = 0;
-#pragma unroll 1
-  for (int r = 0; r < kTopK; ++r) {
-    uint64_t best = 0;
+  auto lane_best = [&](uint32_t& key, int& slot) {
+    key = 0;
+    slot = 0;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const float v = keep ? sb[i] : -3.402823466e38f;
-      const uint64_t key = (static_cast<uint64_t>(orderable(v)) << 32) |
-                           static_cast<uint64_t>(0xFFFFu - (lane * 8 + i));
-      const bool free_slot = ((taken >> i) & 1u) == 0;
-      if (free_slot && key > best) best = key;
+      const uint32_t k = keep && !((taken >> i) & 1u) ? orderable(sb[i]) : 0u;
+      if (k > key) {
+        key = k;
+        slot = i;
+      }
     }
-#pragma unroll
-    for (int d = 16; d >= 1; d >>= 1) {
-      const uint64_t o = __shfl_xor_sync(0xffffffffu, best, d);
-      best = o > best ? o : best;
+  };
+  uint32_t bkey;
+  int bslot;
+  lane_best(bkey, bslot);
+#pragma unroll 1
+  for (int r = 0; r < kTopK; ++r) {
+    const uint32_t m = __reduce_max_sync(0xffffffffu, bkey);
+    const uint32_t holders = __ballot_sync(0xffffffffu, bkey == m);
+    if (lane == __ffs(holders) - 1) {
+      taken |= 1u << bslot;
+      lane_best(bkey, bslot);
     }
-    const int id = 0xFFFF - static_cast<int>(best & 0xFFFFu);
-    if ((id >> 3) == lane) taken |= 1u << (id & 7);
   }
   // combine weights from s (no bias): s / (sum + 1e-20) * rsf (reference_official.py:122-126)
   float part = 0.f;
@@ -400,7 +407,6 @@ __device__ void scan_plan(const RouteArgs& a, int* s_tmp, int* s_start) {
 
 __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
   __shared__ float s_bias[kEG];
-  __shared__ uint32_t s_mask[kEG][kChunk / 32];
   __shared__ int s_tmp[1024];
   __shared__ int s_start[kEG];
   __shared__ int s_last;
@@ -420,10 +426,6 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
   __threadfence();
   scan_plan(a, s_tmp, s_start);
   if (tid == 0) *a.route_done = 0;   // self-reset for the next call
-  if (a.nchunks == 1) {
-    build_chunk_masks(a, 0, s_mask);
-    for (int tl = warp; tl < a.T; tl += kRouteWarps) scatter_token(a, tl, tl, lane, s_mask, s_start);
-  }
 }
 
 __global__ void __launch_bounds__(kRouteThreads) scatter_kernel(RouteArgs a) {
@@ -439,9 +441,12 @@ __global__ void __launch_bounds__(kRouteThreads) scatter_kernel(RouteArgs a) {
   if (t < a.T) scatter_token(a, t, t - c * kChunk, lane, s_mask, s_base);
 }
 
-// T <= kRouteSmallT: one CTA of 32 warps routes every token, scans and scatters in a single
-// launch (the decode regime, where the routing latency is on the layer's critical path).
-constexpr int kRouteSmallT = 256;
+// T <= kRouteSmallT: one CTA routes every token (one warp each, a single round), scans and
+// scatters in a single launch -- the decode regime, where a second launch would cost more than
+// it saves.  Larger batches spread the tokens over T/8 CTAs (a warp's routing of one token is a
+// serial chain of several thousand cycles, and one SM would take T/32 of them in turn) and
+// permute with scatter_kernel on as many CTAs.
+constexpr int kRouteSmallT = 32;
 constexpr int kRouteSmallThreads = 1024;
 
 __device__ __forceinline__ void route_small_body(const RouteArgs& a) {
@@ -479,10 +484,8 @@ cudaError_t route_launch(const RouteArgs& a, cudaStream_t st, int* launches) {
   const int grid = (a.T + kRouteWarps - 1) / kRouteWarps;
   route_kernel<<<grid, kRouteThreads, 0, st>>>(a);
   ++*launches;
-  if (a.nchunks > 1) {
-    scatter_kernel<<<grid, kRouteThreads, 0, st>>>(a);
-    ++*launches;
-  }
+  scatter_kernel<<<grid, kRouteThreads, 0, st>>>(a);
+  ++*launches;
   return cudaGetLastError();
 }
 
