@@ -25,6 +25,7 @@ cudaError_t combine_launch(int T, int grid, cudaStream_t st, const int* tok_nloc
                            const float* part2, uint16_t* out);
 cudaError_t stream_launch(int mode, int grid, cudaStream_t st, const CUtensorMap& w, const CUtensorMap& t,
                           const CUtensorMap& t2, const TileArgs& g);
+cudaError_t stream_fin_launch(int G, cudaStream_t st, const TileArgs& g);
 
 }  // namespace moe
 
@@ -335,6 +336,9 @@ int forward_impl(const moe_b200_args* a, void* workspace, size_t ws_bytes, void*
     s1.trace = trace;
     cudaError_t e = moe::stream_launch(1, grid, st, mW13s, mTok, mTok, s1);
     if (e != cudaSuccess) return cuda_fail(e, "stream gemm1 launch");
+    ++launches;
+    e = moe::stream_fin_launch(grid, st, s1);
+    if (e != cudaSuccess) return cuda_fail(e, "stream gemm1 finish launch");
     ++launches;
     if (ev) cudaEventRecord(ev[2], st);
     moe::TileArgs s2 = s;

@@ -9,7 +9,10 @@
 //       D1 = W13[X1 rows] . A^T,  D2 = W13[X2 rows] . A^T   (fp8 x fp8 -> fp32 TMEM)
 //       acc_i[r][c] += D_i[r][c] * s13[e, block_i, kb] * sa[token c, kb]   (exact fp32 scales)
 //     epilogue: C = silu(X2) * X1 per (feature r, token c); per-token amax over the tile's
-//     128 features; C stored as the hi/lo e4m3 pair C ~= s*(hi + lo/16), s = amax/448.
+//     128 features; C stored as the hi/lo e4m3 pair C ~= s*(hi + lo/16), s = amax/448.  A tile
+//     that stream-K split over several CTAs is summed and finished by stream_fin1_kernel, a
+//     programmatic dependent of this kernel, so no CTA's range ends with a wait-free but
+//     latency-bound fixup and epilogue on the critical path.
 //   MODE 2 (GEMM2): tile = (expert, 32-token tile, 128 output features nt); K = 16 blocks.
 //       D_hi = W2 . C_hi^T,  D_lo = W2 . C_lo^T
 //       acc[r][c] += (D_hi + D_lo/16)[r][c] * s2[e, nt, kb] * sc[token c, kb]
@@ -101,8 +104,8 @@ struct STile {
   int e, nt, row0, nr;
 };
 
-template <int MODE>
-__device__ __forceinline__ STile s_decode(const StreamSmem<MODE>& sm, int E, int tile) {
+template <int MODE, class SM>
+__device__ __forceinline__ STile s_decode(const SM& sm, int E, int tile) {
   constexpr int NT = SCfg<MODE>::NT;
   int lo = 0, hi = E - 1;
   while (lo < hi) {
@@ -267,8 +270,8 @@ done:
 }
 
 // MODE 1 tile epilogue: SwiGLU, per-token amax over the 128 features, hi/lo e4m3 encoding.
-__device__ void s_epi1(StreamSmem<1>& sm, const TileArgs& g, const STile& s, float* x1, const float* x2,
-                       int q, int lane) {
+template <class SM>
+__device__ void s_epi1(SM& sm, const TileArgs& g, const STile& s, float* x1, const float* x2, int q, int lane) {
   const int r = q * 32 + lane;
   float m[kTok];
 #pragma unroll
@@ -418,6 +421,19 @@ __device__ void s_epilogue(StreamSmem<MODE>& sm, uint32_t tmem, const TileArgs& 
     }
     t0 = MOE_TCLK();
     const bool full = (k0 == 0 && k1 == SCfg<MODE>::KB);
+    if (MODE == 1 && !full) {
+      // GEMM1: leave the partial for stream_fin1_kernel, which sums the contributors of every
+      // split tile after this kernel, so no CTA ends its range waiting on the slowest one
+      const int slot = sk.slot(blockIdx.x, tile);
+      float* p = g.part + static_cast<size_t>(slot) * 2 * kTok * 128;
+#pragma unroll
+      for (int c = 0; c < kTok; ++c) {
+        p[c * 128 + r] = acc1[c];
+        p[(kTok + c) * 128 + r] = acc2[c];
+      }
+      MOE_TADD(tf, t0);
+      continue;
+    }
     if (!full) {
       // stream-K fixup: publish this CTA's partial, the last contributor sums them in CTA order
       constexpr int NH = MODE == 1 ? 2 : 1;
@@ -556,6 +572,73 @@ cudaError_t stream_prepare() {
 }
 
 // Launched as programmatic dependents of the preceding kernel in the stream (PDL).
+// Shared memory of stream_fin1_kernel: the tile tables and the MODE 1 epilogue's buffers.
+struct FinSmem {
+  uint8_t ostage[2][kTok][128];
+  float colmax[4][kTok];
+  float amax[kTok];
+  int e_cnt[kEG + 1];
+  int e_start[kEG + 1];
+  int e_tt[kEG + 1];
+};
+
+// GEMM1 tiles that stream-K split over several CTAs: the contributors' partial accumulators
+// summed in CTA order (deterministic; the same sums in the same order as a last-arriver fixup)
+// followed by the tile epilogue (SwiGLU, hi/lo e4m3).  One CTA of 128 threads per split tile,
+// thread = weight row; G is the GEMM's grid, which fixes its tile split.
+__global__ void __launch_bounds__(kSEpiThreads) stream_fin1_kernel(TileArgs g, int G) {
+  __shared__ FinSmem sm;
+  pdl_wait();                 // the partials come from GEMM1
+  pdl_launch_dependents();    // GEMM2 may start its prologue and weight prefetch
+  const Plan plan = *g.plan;
+  Sched sk;
+  sk.init(plan.tt * SCfg<1>::NT, G, SCfg<1>::KB);
+  const int nsplit = sk.tiles - sk.dp;   // stream-K tiles
+  if (static_cast<int>(blockIdx.x) >= nsplit) return;
+  for (int i = threadIdx.x; i <= g.E; i += blockDim.x) {
+    sm.e_cnt[i] = i < g.E ? g.e_count[i] : 0;
+    sm.e_start[i] = g.e_start[i];
+    sm.e_tt[i] = g.e_tiles[i];
+  }
+  __syncthreads();
+  const int q = threadIdx.x >> 5, lane = threadIdx.x & 31, r = threadIdx.x;
+  for (int i = blockIdx.x; i < nsplit; i += gridDim.x) {
+    const int tile = sk.dp + i;
+    const int c0 = sk.first_cta(tile), c1 = sk.last_cta(tile);
+    if (c0 == c1) continue;   // one contributor: the GEMM finished this tile itself
+    const STile s = s_decode<1>(sm, g.E, tile);
+    float acc1[kTok], acc2[kTok];
+#pragma unroll
+    for (int c = 0; c < kTok; ++c) {
+      acc1[c] = 0.f;
+      acc2[c] = 0.f;
+    }
+    for (int cta = c0; cta <= c1; ++cta) {
+      const float* pp = g.part + static_cast<size_t>(sk.slot(cta, tile)) * 2 * kTok * 128;
+#pragma unroll
+      for (int c = 0; c < kTok; ++c) {
+        acc1[c] += __ldcg(pp + c * 128 + r);
+        acc2[c] += __ldcg(pp + (kTok + c) * 128 + r);
+      }
+    }
+    s_epi1(sm, g, s, acc1, acc2, q, lane);
+  }
+}
+
+// Launched as a programmatic dependent of GEMM1.
+cudaError_t stream_fin_launch(int G, cudaStream_t st, const TileArgs& g) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(G);
+  cfg.blockDim = dim3(kSEpiThreads);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, stream_fin1_kernel, g, G);
+}
+
 cudaError_t stream_launch(int mode, int grid, cudaStream_t st, const CUtensorMap& w, const CUtensorMap& t,
                           const CUtensorMap& t2, const TileArgs& g) {
   cudaLaunchConfig_t cfg = {};
