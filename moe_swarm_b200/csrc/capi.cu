@@ -358,8 +358,8 @@ int forward_impl(const moe_b200_args* a, void* workspace, size_t ws_bytes, void*
   CUtensorMap mA1, mW13, mChi, mClo, mW2;
   if (!encode_u8_2d(&mA1, ws + L.a_perm, moe::kH, L.r_pad, 128) ||
       !encode_u8_2d(&mW13, a->gemm1_weights, moe::kH, (uint64_t)E * moe::kN1) ||
-      !encode_u8_2d(&mChi, ws + L.c_hi, moe::kI, L.r_pad, 16) ||
-      !encode_u8_2d(&mClo, ws + L.c_lo, moe::kI, L.r_pad, 16) ||
+      !encode_u8_2d(&mChi, ws + L.c_hi, moe::kI, L.r_pad, 128) ||
+      !encode_u8_2d(&mClo, ws + L.c_lo, moe::kI, L.r_pad, 128) ||
       !encode_u8_2d(&mW2, a->gemm2_weights, moe::kI, (uint64_t)E * moe::kH))
     return fail(MOE_B200_ERR_CUDA, "cuTensorMapEncodeTiled failed");
   moe::TileArgs w = tile_args(a, ws, L);
@@ -375,7 +375,7 @@ int forward_impl(const moe_b200_args* a, void* workspace, size_t ws_bytes, void*
   ++launches;
   if (ev) cudaEventRecord(ev[2], st);
   moe::TileArgs w2 = w;
-  w2.e_tiles = reinterpret_cast<const int*>(ws + L.e_m64);
+  w2.e_tiles = reinterpret_cast<const int*>(ws + L.e_mt_start);
   w2.sa = reinterpret_cast<const float*>(ws + L.c_scale);
   w2.sw = a->gemm2_weights_scale;
   w2.trace = trace + 3 * (size_t)moe::kMaxSms * moe::kTraceSlots;

@@ -9,13 +9,14 @@
 //       D1 = W13[X1 rows] . A^T,  D2 = W13[X2 rows] . A^T   (fp8 x fp8 -> fp32 TMEM)
 //       acc_i[r][c] += D_i[r][c] * s13[e, block_i, kb] * sa[token c, kb]   (exact fp32 scales)
 //     epilogue: C = silu(X2) * X1 per (feature r, token c); per-token amax over the tile's
-//     128 features; C stored as the hi/lo e4m3 pair C ~= s*(hi + lo/16), s = amax/448.  A tile
+//     128 features; C stored as the e4m3 pair C ~= s*(hi + lo), hi = e4m3(C/s), lo =
+//     e4m3(C/s - hi), s = amax/448.  A tile
 //     that stream-K split over several CTAs is summed and finished by stream_fin1_kernel, a
 //     programmatic dependent of this kernel, so no CTA's range ends with a wait-free but
 //     latency-bound fixup and epilogue on the critical path.
 //   MODE 2 (GEMM2): tile = (expert, 32-token tile, 128 output features nt); K = 16 blocks.
-//       D_hi = W2 . C_hi^T,  D_lo = W2 . C_lo^T
-//       acc[r][c] += (D_hi + D_lo/16)[r][c] * s2[e, nt, kb] * sc[token c, kb]
+//       D = W2 . C_hi^T + W2 . C_lo^T   (one accumulator: hi and lo share every scale)
+//       acc[r][c] += D[r][c] * s2[e, nt, kb] * sc[token c, kb]
 //     epilogue: out[t, f] = bf16(w * O) for a token with one local expert; otherwise the
 //     token's rows are summed in ascending expert order by the last contributing tile
 //     (per-(token, 128-feature) arrival counter) -- deterministic.
@@ -244,7 +245,7 @@ __device__ void s_mma(StreamSmem<MODE>& sm, uint32_t tmem, const TileArgs& g, co
           } else {
             const uint64_t aw = sdesc_k128_sw128(st + 32 * k);
             mma_f8f6f4(d, aw, sdesc_k128_sw128(st + 16384 + 32 * k), idesc, k > 0);
-            mma_f8f6f4(d + 32u, aw, sdesc_k128_sw128(st + 16384 + kTok * 128 + 32 * k), idesc, k > 0);
+            mma_f8f6f4(d, aw, sdesc_k128_sw128(st + 16384 + kTok * 128 + 32 * k), idesc, 1);
           }
         }
       }
@@ -297,7 +298,7 @@ __device__ void s_epi1(SM& sm, const TileArgs& g, const STile& s, float* x1, con
     const float y1 = x1[c + 1] * (a1 > 0.f ? 448.0f / a1 : 0.f);
     const uint32_t h = cvt_e4m3x2(y0, y1);
     const float2 b = e4m3x2_to_f2(static_cast<uint16_t>(h));
-    const uint32_t l = cvt_e4m3x2((y0 - b.x) * 16.f, (y1 - b.y) * 16.f);
+    const uint32_t l = cvt_e4m3x2(y0 - b.x, y1 - b.y);
     sm.ostage[0][c][r] = static_cast<uint8_t>(h & 0xFF);
     sm.ostage[0][c + 1][r] = static_cast<uint8_t>(h >> 8);
     sm.ostage[1][c][r] = static_cast<uint8_t>(l & 0xFF);
@@ -398,7 +399,10 @@ __device__ void s_epilogue(StreamSmem<MODE>& sm, uint32_t tmem, const TileArgs& 
       if (!dead) {
         tc_fence_after();
         float d1[kTok], d2[kTok];
-        tmem_ld32x2_wait(lane_base + buf * 64u, lane_base + buf * 64u + 32u, d1, d2);
+        if (MODE == 1)
+          tmem_ld32x2_wait(lane_base + buf * 64u, lane_base + buf * 64u + 32u, d1, d2);
+        else
+          tmem_ld16x2_wait(lane_base + buf * 64u, lane_base + buf * 64u + 16u, d1, d1 + 16);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.tempty[buf]);
@@ -411,7 +415,7 @@ __device__ void s_epilogue(StreamSmem<MODE>& sm, uint32_t tmem, const TileArgs& 
             acc1[c] = fmaf(d1[c], sc * w1, acc1[c]);
             acc2[c] = fmaf(d2[c], sc * w2, acc2[c]);
           } else {
-            acc1[c] = fmaf(fmaf(d2[c], 0.0625f, d1[c]), sc * w1, acc1[c]);
+            acc1[c] = fmaf(d1[c], sc * w1, acc1[c]);
           }
         }
       }

@@ -6,21 +6,22 @@
 //   MODE 1 (GEMM1): tile = (expert, 128-row token tile, pair tile nt: 128 X1 rows [128nt, +128)
 //     and 128 X2 rows [2048+128nt, +128)); K = 56 blocks.  D = A . [W_X1 | W_X2]^T.
 //       acc[r][c] += D[r][c] * sa[r, kb] * s13[e, block(c), kb]
-//     epilogue: C = silu(X2) * X1, stored as the hi/lo e4m3 pair C ~= s*(hi + lo/16) with one
-//     scale per (row, 128 columns), s = amax/448.
-//   MODE 2 (GEMM2): tile = (expert, 64-token tile, 256 output features nt); K = 16 blocks.
-//     The A tile holds each token twice, as its hi row and its lo row, interleaved in groups
-//     of 16 so that a token's two rows sit in one TMEM lane quarter: smem/TMEM row
-//     32q + i (i < 16) is hi of token 16q + i, row 32q + 16 + i is lo of the same token.
-//       acc[r][c] += D[r][c] * sc[token(r), kb] * s2[e, nt, kb] * (lo ? 1/16 : 1)
-//     epilogue: one shuffle adds a token's lo half to its hi half; a token with one local
-//     expert gets its bf16 output row directly, otherwise w * O goes to its fp32 partial row,
-//     summed in ascending expert order by the combine kernel (combine.cu).
+//     epilogue: C = silu(X2) * X1, stored as the e4m3 pair C ~= s*(hi + lo), hi = e4m3(C/s),
+//     lo = e4m3(C/s - hi), with one scale per (row, 128 columns), s = amax/448.
+//   MODE 2 (GEMM2): tile = (expert, 128-token tile, 256 output features nt); K = 16 blocks.
+//     hi and lo share every scale, so a K-block is one accumulation over the concatenation
+//     [hi | lo]: four MMAs with A = hi, then four with A = lo, into the same accumulator.
+//       acc[r][c] += D[r][c] * sc[token r, kb] * s2[e, nt, kb]
+//     epilogue: a token with one local expert gets its bf16 output row directly, otherwise
+//     w * O goes to its fp32 partial row, summed in ascending expert order by the combine
+//     kernel (combine.cu).
 //
 // CTA = 12 warps: warp 0 TMA producer (one box per lane), warp 1 TMEM owner + single-thread MMA
 // issuer (their warpgroup drops to 56 registers), warps 4..11 promotion/epilogue with 224
-// registers: two warps per TMEM lane quarter, one per column half.
-// 4 smem stages of 48 KB, 2 TMEM accumulator buffers of 256 columns.  Work: data-parallel
+// registers: two warps per TMEM lane quarter, one per 128-column half of the accumulator.
+// Shared-memory stages: MODE 1 4 x 48 KB (128 token rows | 128 X1 rows | 128 X2 rows),
+// MODE 2 3 x 64 KB (128 hi rows | 128 lo rows | 256 W2 rows); 2 TMEM accumulator buffers of 256
+// columns.  Work: data-parallel
 // whole tiles, then a stream-K tail (sched.cuh).  No TMA multicast (the kernels also run in the
 // multi-GPU expert-parallel configuration).
 #include <cuda.h>
@@ -48,24 +49,26 @@ template <>
 struct WCfg<1> {
   static constexpr int KB = kKB1;
   static constexpr int NT = kNT1;     // 16 pair tiles
-  static constexpr int ROWS = 128;    // token rows per tile
+  static constexpr int STAGES = 4;
+  static constexpr int STAGE_BYTES = 3 * 16384;
 };
 template <>
 struct WCfg<2> {
   static constexpr int KB = kKB2;
   static constexpr int NT = kH / 256; // 28 feature tiles of 256
-  static constexpr int ROWS = 64;
+  static constexpr int STAGES = 3;
+  static constexpr int STAGE_BYTES = 4 * 16384;
 };
+constexpr int kWRows = 128;      // token rows per tile (MMA M)
 
-constexpr int kWStages = 4;
-constexpr int kWStageBytes = 3 * 16384;
 constexpr int kWThreads = 384;   // 3 warpgroups: producer/MMA (+2 idle warps), 2 x epilogue
 constexpr int kWEpiThreads = 256;
 
+template <int MODE>
 struct WideSmem {
-  uint8_t stage[kWStages][kWStageBytes];
-  uint64_t full[kWStages];
-  uint64_t empty[kWStages];
+  uint8_t stage[WCfg<MODE>::STAGES][WCfg<MODE>::STAGE_BYTES];
+  uint64_t full[WCfg<MODE>::STAGES];
+  uint64_t empty[WCfg<MODE>::STAGES];
   uint64_t tfull[2];
   uint64_t tempty[2];
   uint64_t drain;
@@ -76,21 +79,25 @@ struct WideSmem {
   float amx[2][128];       // MODE 1: per-row amax of each column half
   // per-epilogue-warp staging of output rows so each warp store writes whole row segments
   alignas(16) uint8_t ostg[8][2560];
-  int mt[8][16];           // MODE 2: per-warp row metadata (token, local expert count)
+  int mt[8][32];           // MODE 2: per-warp row metadata (output row or partial row)
   int e_cnt[kEG + 1];
   int e_start[kEG + 1];
   int e_tiles[kEG + 1];
 };
 
-constexpr size_t kWideSmemBytes = sizeof(WideSmem) + 1024;
+template <int MODE>
+constexpr size_t wide_smem_bytes() {
+  return sizeof(WideSmem<MODE>) + 1024;
+}
+static_assert(wide_smem_bytes<1>() <= 232448 && wide_smem_bytes<2>() <= 232448, "wide kernel shared memory");
 
 struct WTile {
   int e, nt, row0, nr;
 };
 
 template <int MODE>
-__device__ __forceinline__ WTile w_decode(const WideSmem& sm, int E, int tile) {
-  constexpr int NT = WCfg<MODE>::NT, ROWS = WCfg<MODE>::ROWS;
+__device__ __forceinline__ WTile w_decode(const WideSmem<MODE>& sm, int E, int tile) {
+  constexpr int NT = WCfg<MODE>::NT, ROWS = kWRows;
   int lo = 0, hi = E - 1;
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
@@ -114,25 +121,19 @@ __device__ __forceinline__ uint32_t bf16x2_bits(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&b);
 }
 
-// One box of a MODE 2 token tile: box j < 8 is hi (even j) or lo (odd j) of row group j / 2.
-__device__ __forceinline__ void w_load_c(uint8_t* st, const CUtensorMap* tmA, const CUtensorMap* tmA2, uint64_t* bar,
-                                         int kb, int row0, int j) {
-  const int q = j >> 1;
-  tma_load_2d(st + q * 4096 + (j & 1) * 2048, (j & 1) ? tmA2 : tmA, bar, kb * kBlk, row0 + 16 * q);
-}
-
 // The whole producer warp runs this loop; each lane issues at most one box of a stage.  Tiled
 // loads issued by one thread go through the TMA unit one after another (about 330 cycles per
 // 16 KB box); issued by several lanes of a warp they overlap.
 template <int MODE>
-__device__ __forceinline__ void w_producer(WideSmem& sm, const CUtensorMap* tmA, const CUtensorMap* tmA2,
+__device__ __forceinline__ void w_producer(WideSmem<MODE>& sm, const CUtensorMap* tmA, const CUtensorMap* tmA2,
                            const CUtensorMap* tmB, const TileArgs& g, const Sched& sk, int lane) {
+  constexpr int ST = WCfg<MODE>::STAGES;
   uint32_t stage = 0, phase = 0, issued = 0, lastpar = 0;
   long long tw = 0, nkb = 0;
   // MODE 2: the first stages get their weight tiles before the dependency on GEMM1 resolves
   int pend_n = 0;
-  int pend_row0[kWStages];
-  int pend_kb[kWStages];
+  int pend_row0[ST];
+  int pend_kb[ST];
   bool waited = MODE == 1;
   SegIter it(sk, blockIdx.x);
   int tile, k0, k1;
@@ -145,7 +146,7 @@ __device__ __forceinline__ void w_producer(WideSmem& sm, const CUtensorMap* tmA,
       MOE_WADD(tw, t0);
       ++nkb;
       // the stage's byte count is armed before any lane's copy can complete it
-      if (lane == 0) mbar_arrive_expect_tx(&sm.full[stage], kWStageBytes);
+      if (lane == 0) mbar_arrive_expect_tx(&sm.full[stage], WCfg<MODE>::STAGE_BYTES);
       __syncwarp();
       uint8_t* st = sm.stage[stage];
       if (MODE == 1) {
@@ -153,27 +154,28 @@ __device__ __forceinline__ void w_producer(WideSmem& sm, const CUtensorMap* tmA,
         if (lane == 1) tma_load_2d(st + 16384, tmB, &sm.full[stage], kb * kBlk, s.e * kN1 + s.nt * kBlk);
         if (lane == 2) tma_load_2d(st + 32768, tmB, &sm.full[stage], kb * kBlk, s.e * kN1 + kI + s.nt * kBlk);
       } else {
-        if (lane == 8) tma_load_2d(st + 16384, tmB, &sm.full[stage], kb * kBlk, s.e * kH + s.nt * 256);
-        if (lane == 9) tma_load_2d(st + 32768, tmB, &sm.full[stage], kb * kBlk, s.e * kH + s.nt * 256 + 128);
+        if (lane == 2) tma_load_2d(st + 32768, tmB, &sm.full[stage], kb * kBlk, s.e * kH + s.nt * 256);
+        if (lane == 3) tma_load_2d(st + 49152, tmB, &sm.full[stage], kb * kBlk, s.e * kH + s.nt * 256 + 128);
         if (!waited) {
           pend_row0[pend_n] = s.row0;
           pend_kb[pend_n] = kb;
           ++pend_n;
-        } else if (lane < 8) {
-          w_load_c(st, tmA, tmA2, &sm.full[stage], kb, s.row0, lane);
+        } else if (lane < 2) {
+          tma_load_2d(st + 16384 * lane, lane ? tmA2 : tmA, &sm.full[stage], kb * kBlk, s.row0);
         }
       }
       issued |= 1u << stage;
       lastpar = (lastpar & ~(1u << stage)) | (phase << stage);
-      if (++stage == kWStages) {
+      if (++stage == ST) {
         stage = 0;
         phase ^= 1u;
       }
-      if (MODE == 2 && !waited && pend_n == kWStages) {
+      if (MODE == 2 && !waited && pend_n == ST) {
         pdl_wait();
         waited = true;
         for (int i = 0; i < pend_n; ++i)
-          if (lane < 8) w_load_c(sm.stage[i], tmA, tmA2, &sm.full[i], pend_kb[i], pend_row0[i], lane);
+          if (lane < 2)
+            tma_load_2d(sm.stage[i] + 16384 * lane, lane ? tmA2 : tmA, &sm.full[i], pend_kb[i] * kBlk, pend_row0[i]);
         pend_n = 0;
       }
     }
@@ -181,11 +183,12 @@ __device__ __forceinline__ void w_producer(WideSmem& sm, const CUtensorMap* tmA,
   if (MODE == 2 && !waited) {
     pdl_wait();
     for (int i = 0; i < pend_n; ++i)
-      if (lane < 8) w_load_c(sm.stage[i], tmA, tmA2, &sm.full[i], pend_kb[i], pend_row0[i], lane);
+      if (lane < 2)
+        tma_load_2d(sm.stage[i] + 16384 * lane, lane ? tmA2 : tmA, &sm.full[i], pend_kb[i] * kBlk, pend_row0[i]);
   }
 drain:
   if (lane == 0)
-    for (int s = 0; s < kWStages; ++s)
+    for (int s = 0; s < ST; ++s)
       if ((issued >> s) & 1u) {
         int no_abort = 0;
         mbar_wait(&sm.full[s], (lastpar >> s) & 1u, &no_abort, g.status, kStWaitDrain);
@@ -199,7 +202,9 @@ drain:
 #endif
 }
 
-__device__ __forceinline__ void w_mma(WideSmem& sm, uint32_t tmem, const TileArgs& g, const Sched& sk) {
+template <int MODE>
+__device__ __forceinline__ void w_mma(WideSmem<MODE>& sm, uint32_t tmem, const TileArgs& g, const Sched& sk) {
+  constexpr int ST = WCfg<MODE>::STAGES;
   constexpr uint32_t idesc = idesc_e4m3_f32(128, 256);
   uint32_t stage = 0, phase = 0, tk = 0, buf = 0;
   long long tw_t = 0, tw_f = 0, t_first = 0;
@@ -221,15 +226,23 @@ __device__ __forceinline__ void w_mma(WideSmem& sm, uint32_t tmem, const TileArg
       {
         const uint32_t st = smem_u32(sm.stage[stage]);
         const uint32_t d = tmem + buf * 256u;
+        if (MODE == 1) {
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-          mma_f8f6f4(d, sdesc_k128_sw128(st + 32 * k), sdesc_k128_sw128(st + 16384 + 32 * k), idesc, k > 0);
+          for (int k = 0; k < 4; ++k)
+            mma_f8f6f4(d, sdesc_k128_sw128(st + 32 * k), sdesc_k128_sw128(st + 16384 + 32 * k), idesc, k > 0);
+        } else {
+          // D = hi . W^T + lo . W^T over the K-block: A = hi, then A = lo, one accumulator
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            mma_f8f6f4(d, sdesc_k128_sw128(st + 16384 * (k >> 2) + 32 * (k & 3)),
+                       sdesc_k128_sw128(st + 32768 + 32 * (k & 3)), idesc, k > 0);
+        }
       }
       mma_commit(&sm.empty[stage]);
       mma_commit(&sm.tfull[buf]);
       tk ^= 1u << buf;
       buf ^= 1u;
-      if (++stage == kWStages) {
+      if (++stage == ST) {
         stage = 0;
         phase ^= 1u;
       }
@@ -248,7 +261,7 @@ done:
 
 // MODE 1 tile epilogue: SwiGLU of this thread's 64 (X1, X2) column pairs of row `rit`, the row's
 // 128-column amax (exchanged with the other column half), hi/lo e4m3 encoding and stores.
-__device__ __forceinline__ void w_epi1(WideSmem& sm, const TileArgs& g, const WTile& s, float* x1,
+__device__ __forceinline__ void w_epi1(WideSmem<1>& sm, const TileArgs& g, const WTile& s, float* x1,
                                        const float* x2, int h, int rit, uint32_t* hw, uint32_t* lw) {
   float amax = 0.f;
 #pragma unroll
@@ -266,8 +279,8 @@ __device__ __forceinline__ void w_epi1(WideSmem& sm, const TileArgs& g, const WT
     const uint32_t h01 = cvt_e4m3x2(y0, y1), h23 = cvt_e4m3x2(y2, y3);
     const float2 b01 = e4m3x2_to_f2(static_cast<uint16_t>(h01));
     const float2 b23 = e4m3x2_to_f2(static_cast<uint16_t>(h23));
-    const uint32_t l01 = cvt_e4m3x2((y0 - b01.x) * 16.f, (y1 - b01.y) * 16.f);
-    const uint32_t l23 = cvt_e4m3x2((y2 - b23.x) * 16.f, (y3 - b23.y) * 16.f);
+    const uint32_t l01 = cvt_e4m3x2(y0 - b01.x, y1 - b01.y);
+    const uint32_t l23 = cvt_e4m3x2(y2 - b23.x, y3 - b23.y);
     hw[j / 4] = h01 | (h23 << 16);
     lw[j / 4] = l01 | (l23 << 16);
   }
@@ -277,7 +290,7 @@ __device__ __forceinline__ void w_epi1(WideSmem& sm, const TileArgs& g, const WT
 
 // Stores this warp's 32 rows x 64 bytes (hi, then lo) through its staging buffer: each lane
 // stages its row, then every warp store writes 8 whole 64-byte row segments.
-__device__ __forceinline__ void w_store1(WideSmem& sm, const TileArgs& g, const WTile& s, const uint32_t* hw,
+__device__ __forceinline__ void w_store1(WideSmem<1>& sm, const TileArgs& g, const WTile& s, const uint32_t* hw,
                                          const uint32_t* lw, int ew, int q, int h, int lane) {
   uint8_t* st = sm.ostg[ew];
   const int rows_here = min(32, s.nr - 32 * q);   // valid rows of this warp's quarter
@@ -301,38 +314,34 @@ __device__ __forceinline__ void w_store1(WideSmem& sm, const TileArgs& g, const 
   }
 }
 
-// MODE 2 tile epilogue: hi + lo, then this thread's 128 output columns of token `tok` (lanes
-// 0..15 of each quarter): the bf16 output row directly for a token with one local expert,
-// otherwise the routing-weighted fp32 row for the combine kernel.
-__device__ __forceinline__ void w_epi2(WideSmem& sm, const TileArgs& g, const WTile& s, float* acc, int ew, int h,
-                                       int q, int lane, int t, float w, int kt) {
-#pragma unroll
-  for (int j = 0; j < 128; ++j) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], 16);
-  // lanes 0..15 own token rows 16q + lane; each warp writes its 16 rows x 128 columns in four
-  // rounds of 32 columns staged through shared memory, 4 whole 128-byte row segments per store
-  const int rows_here = min(16, s.nr - 16 * q);
-  float* st = reinterpret_cast<float*>(sm.ostg[ew]);   // [16][36]
-  if (lane < 16) sm.mt[ew][lane] = kt == 1 ? -1 - t : t;   // < 0: the bf16 output row of token -1-v
+// MODE 2 tile epilogue: this thread's 128 output columns of its token row: the bf16 output row
+// directly for a token with one local expert, otherwise the routing-weighted fp32 row for the
+// combine kernel.  Each warp writes its 32 rows x 128 columns in eight rounds of 16 columns
+// staged through shared memory, 8 whole 64-byte (fp32) row segments per store.
+__device__ __forceinline__ void w_epi2(WideSmem<2>& sm, const TileArgs& g, const WTile& s, const float* acc, int ew,
+                                       int h, int q, int lane, int t, float w, int kt) {
+  const int rows_here = min(32, s.nr - 32 * q);
+  float* st = reinterpret_cast<float*>(sm.ostg[ew]);   // [32][20]
+  sm.mt[ew][lane] = kt == 1 ? -1 - t : t;              // < 0: the bf16 output row of token -1-v
   const int col0 = s.nt * 256 + 128 * h;
+  __syncwarp();
 #pragma unroll
-  for (int rd = 0; rd < 4; ++rd) {
-    if (lane < 16) {
+  for (int rd = 0; rd < 8; ++rd) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) st[lane * 36 + j] = __fmul_rn(acc[32 * rd + j], w);
-    }
+    for (int j = 0; j < 16; ++j) st[lane * 20 + j] = __fmul_rn(acc[16 * rd + j], w);
     __syncwarp();
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const int r = 4 * i + (lane >> 3), ch = lane & 7;
+      const int r = 8 * i + (lane >> 2), ch = lane & 3;
       if (r < rows_here) {
-        const float4 v = *reinterpret_cast<const float4*>(st + r * 36 + 4 * ch);
+        const float4 v = *reinterpret_cast<const float4*>(st + r * 20 + 4 * ch);
         const int tv = sm.mt[ew][r];
-        const int col = col0 + 32 * rd + 4 * ch;
+        const int col = col0 + 16 * rd + 4 * ch;
         if (tv < 0) {
           *reinterpret_cast<uint2*>(g.out + static_cast<size_t>(-1 - tv) * kH + col) =
               make_uint2(bf16x2_bits(v.x, v.y), bf16x2_bits(v.z, v.w));
         } else {
-          *reinterpret_cast<float4*>(g.part2 + static_cast<size_t>(s.row0 + 16 * q + r) * kH + col) = v;
+          *reinterpret_cast<float4*>(g.part2 + static_cast<size_t>(s.row0 + 32 * q + r) * kH + col) = v;
         }
       }
     }
@@ -341,7 +350,7 @@ __device__ __forceinline__ void w_epi2(WideSmem& sm, const TileArgs& g, const WT
 }
 
 template <int MODE>
-__device__ __forceinline__ void w_epilogue(WideSmem& sm, uint32_t tmem, const TileArgs& g, const Sched& sk, int warp, int lane) {
+__device__ __forceinline__ void w_epilogue(WideSmem<MODE>& sm, uint32_t tmem, const TileArgs& g, const Sched& sk, int warp, int lane) {
   constexpr int KB = WCfg<MODE>::KB;
   const int ew = warp - 4;
   const int q = warp & 3;
@@ -357,16 +366,15 @@ __device__ __forceinline__ void w_epilogue(WideSmem& sm, uint32_t tmem, const Ti
   while (it.next(tile, k0, k1)) {
     const WTile s = w_decode<MODE>(sm, g.E, tile);
     long long t0 = MOE_WCLK();
-    // this thread's token row (MODE 2: lanes l and l+16 share token 16q + (l & 15))
-    const int trow = MODE == 1 ? rit : 16 * q + (lane & 15);
+    // this thread's token row
+    const int trow = rit;
     const size_t srow = static_cast<size_t>(s.row0 + min(trow, s.nr - 1));
-    const float lo_scale = (MODE == 2 && lane >= 16) ? 0.0625f : 1.0f;
     // a lane quarter holding only padding rows skips its TMEM loads and FMAs
-    const bool qlive = (MODE == 1 ? 32 * q : 16 * q) < s.nr;
+    const bool qlive = 32 * q < s.nr;
     // MODE 2: the token metadata of this thread's row, fetched while the K loop runs
     int meta_t = 0, meta_k = 0;
     float meta_w = 0.f;
-    const bool meta_mine = MODE == 2 && lane < 16 && trow < s.nr;
+    const bool meta_mine = MODE == 2 && trow < s.nr;
     if (meta_mine) {
       meta_t = __ldg(g.row_token + s.row0 + trow);
       meta_w = __ldg(g.row_weight + s.row0 + trow);
@@ -442,7 +450,7 @@ __device__ __forceinline__ void w_epilogue(WideSmem& sm, uint32_t tmem, const Ti
             }
           }
         } else {
-          const float f = sa * sm.ssw[h][ki] * lo_scale;
+          const float f = sa * sm.ssw[h][ki];
           const float2 fv = make_float2(f, f);
 #pragma unroll
           for (int c0 = 0; c0 < 128; c0 += 64) {
@@ -524,13 +532,13 @@ __device__ __forceinline__ void w_epilogue(WideSmem& sm, uint32_t tmem, const Ti
     MOE_WADD(tf, t0);
     t0 = MOE_WCLK();
     // (after an abort the epilogue still runs, on garbage, so every warp meets every barrier)
-    if (MODE == 1) {
+    if constexpr (MODE == 1) {
       uint32_t hw[16], lw[16];
       w_epi1(sm, g, s, acc1, acc2, h, rit, hw, lw);
       w_store1(sm, g, s, hw, lw, ew, q, h, lane);
-    }
-    else
+    } else {
       w_epi2(sm, g, s, acc1, ew, h, q, lane, meta_t, meta_w, meta_k);
+    }
     MOE_WADD(te, t0);
   }
 #ifdef MOE_TRACE
@@ -551,13 +559,14 @@ __global__ void __launch_bounds__(kWThreads, 1)
     wide_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA2,
                 const __grid_constant__ CUtensorMap tmB, TileArgs g) {
   extern __shared__ uint8_t smem_raw[];
-  WideSmem& sm = *reinterpret_cast<WideSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  WideSmem<MODE>& sm =
+      *reinterpret_cast<WideSmem<MODE>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   if (MODE == 1) {
     pdl_wait();
     pdl_launch_dependents();
   }
   const Plan plan = *g.plan;
-  const int ntiles = (MODE == 1 ? plan.m_tiles : plan.m64) * WCfg<MODE>::NT;
+  const int ntiles = plan.m_tiles * WCfg<MODE>::NT;
   Sched sk;
   sk.init(ntiles, gridDim.x, WCfg<MODE>::KB);
   if (ntiles == 0 || !sk.has_work(blockIdx.x)) return;
@@ -568,7 +577,7 @@ __global__ void __launch_bounds__(kWThreads, 1)
     sm.e_tiles[i] = g.e_tiles[i];
   }
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kWStages; ++s) {
+    for (int s = 0; s < WCfg<MODE>::STAGES; ++s) {
       mbar_init(&sm.full[s], 1);
       mbar_init(&sm.empty[s], 1);
     }
@@ -600,7 +609,7 @@ __global__ void __launch_bounds__(kWThreads, 1)
     if (warp == 0) {
       w_producer<MODE>(sm, &tmA, &tmA2, &tmB, g, sk, lane);
     } else if (warp == 1) {
-      if (lane == 0) w_mma(sm, tmem, g, sk);
+      if (lane == 0) w_mma<MODE>(sm, tmem, g, sk);
       __syncwarp();
     }
   } else {
@@ -618,10 +627,10 @@ __global__ void __launch_bounds__(kWThreads, 1)
 
 cudaError_t wide_prepare() {
   cudaError_t e = cudaFuncSetAttribute(wide_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(kWideSmemBytes));
+                                       static_cast<int>(wide_smem_bytes<1>()));
   if (e != cudaSuccess) return e;
   return cudaFuncSetAttribute(wide_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              static_cast<int>(kWideSmemBytes));
+                              static_cast<int>(wide_smem_bytes<2>()));
 }
 
 // Launched as programmatic dependents of the preceding kernel in the stream (PDL).
@@ -630,14 +639,17 @@ cudaError_t wide_launch(int mode, int grid, cudaStream_t st, const CUtensorMap& 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kWThreads);
-  cfg.dynamicSmemBytes = kWideSmemBytes;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (mode == 1) return cudaLaunchKernelEx(&cfg, wide_kernel<1>, a, a2, b, g);
+  if (mode == 1) {
+    cfg.dynamicSmemBytes = wide_smem_bytes<1>();
+    return cudaLaunchKernelEx(&cfg, wide_kernel<1>, a, a2, b, g);
+  }
+  cfg.dynamicSmemBytes = wide_smem_bytes<2>();
   return cudaLaunchKernelEx(&cfg, wide_kernel<2>, a, a2, b, g);
 }
 
