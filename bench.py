@@ -221,6 +221,45 @@ def cpu_sample(act_cpu, world, seed=0, k_experts=8, reps=1):
 
 
 # ----------------------------------------------------------------------------- sweeps (N=1)
+def time_calls(M, x, n, flush):
+    """Median device time (µs) of n layer calls, each after an L2 flush."""
+    times = []
+    for _ in range(n):
+        flush.zero_()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        M.run(**x)
+        e.record()
+        e.synchronize()
+        times.append(s.elapsed_time(e) * 1e3)
+    times.sort()
+    return times[len(times) // 2]
+
+
+def roofline_record(f, T, us, peaks_, fp8_peak):
+    """Algorithmic bytes and FLOPs of one call from its routing, achieved rates, and the
+    roofline verdict: the slower of moving the bytes at the measured copy bandwidth and doing the
+    FLOPs at the fp8 peak is the speed-of-light time."""
+    g1, g2 = gemm_bytes(f)
+    byts = g1 + g2 + T * (256 * 4 + 56 * 4)
+    flops = f["rows"] * FLOP_PER_ASSIGN
+    t_hbm = byts / (peaks_["hbm_gbs"] * 1e9)
+    t_fp8 = flops / (fp8_peak * 1e12)
+    floor = max(t_hbm, t_fp8)
+    return {"active_experts": f["active"], "rows": f["rows"], "us": round(us, 1),
+            "tokens_per_s": round(T / (us * 1e-6), 1),
+            "hbm_gbs": round(byts / (us * 1e-6) / 1e9, 1),
+            "hbm_frac": round(byts / (us * 1e-6) / 1e9 / peaks_["hbm_gbs"], 3),
+            "tflops": round(flops / (us * 1e-6) / 1e12, 1),
+            "fp8_frac": round(flops / (us * 1e-6) / 1e12 / fp8_peak, 3),
+            "bound": "hbm" if t_hbm >= t_fp8 else "tensor",
+            "floor_us": round(floor * 1e6, 1),
+            "sol_frac": round(floor / (us * 1e-6), 3)}
+
+
+FP8_PEAK_SOURCE = "2x the measured cuBLAS bf16 burst peak (no measured fp8 peak)"
+
+
 def sweep(device, steps, peaks_):
     import moe_swarm_b200 as M
     import moe_swarm_b200.workload as W
@@ -240,33 +279,47 @@ def sweep(device, steps, peaks_):
         for _ in range(3):
             M.run(**x)
         n = max(5, min(steps, 30)) if T <= 1024 else max(3, min(steps, 10))
-        times = []
+        us = time_calls(M, x, n, flush)
+        # the per-stage split comes from separate calls: events between the kernels break their
+        # programmatic-launch overlap, so those calls are slower than the timed ones
         timer.read(reset=True)
-        for _ in range(n):
+        for _ in range(min(n, 5)):
             flush.zero_()
-            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s.record()
             timer.run(x)
-            e.record()
-            e.synchronize()
-            times.append(s.elapsed_time(e) * 1e3)
+        torch.cuda.synchronize()
         stage_ms, calls = timer.read(reset=True)
-        times.sort()
-        us = times[len(times) // 2]
-        g1, g2 = gemm_bytes(f)
-        byts = g1 + g2 + T * (256 * 4 + 56 * 4)
-        flops = f["rows"] * FLOP_PER_ASSIGN
-        rec = {"workload": name, "T": T, "active_experts": f["active"], "rows": f["rows"], "us": round(us, 1),
-               "tokens_per_s": round(T / (us * 1e-6), 1),
-               "stage_us": {k: round(v * 1e3 / calls, 1) for k, v in zip(("route", "gemm1", "gemm2"), stage_ms)},
-               "hbm_gbs": round(byts / (us * 1e-6) / 1e9, 1),
-               "hbm_frac": round(byts / (us * 1e-6) / 1e9 / peaks_["hbm_gbs"], 3),
-               "tflops": round(flops / (us * 1e-6) / 1e12, 1),
-               "fp8_frac": round(flops / (us * 1e-6) / 1e12 / fp8_peak, 3)}
+        rec = {"workload": name, "T": T}
+        rec.update(roofline_record(f, T, us, peaks_, fp8_peak))
+        rec["stage_us"] = {k: round(v * 1e3 / calls, 1) for k, v in zip(("route", "gemm1", "gemm2"), stage_ms)}
         out.append(rec)
         del x
-    return out, {"fp8_peak_tflops": fp8_peak,
-                 "fp8_peak_source": "2x the measured cuBLAS bf16 burst peak (no measured fp8 peak)"}
+    return out, {"fp8_peak_tflops": fp8_peak, "fp8_peak_source": FP8_PEAK_SOURCE}
+
+
+def replay(args):
+    """--workloads: one JSON line per workload of a flashinfer-bench workload file, timed like
+    the sweeps (median of L2-flushed calls) with the roofline verdict.  Random inputs come from
+    the package's seeded generators; one random-init weight set is shared by all workloads."""
+    import moe_swarm_b200 as M
+    from moe_swarm_b200 import replay as R
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    pk = peaks()
+    fp8_peak = 2.0 * pk["bf16_tflops"]
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    weights = None
+    for wl in R.load(args.workloads):
+        x = R.materialize(wl, args.blob_root, seed=0, device=device, weights=weights)
+        weights = {k: x[k] for k in R.WEIGHTS}
+        f = routing_facts(x)
+        for _ in range(3):
+            M.run(**x)
+        us = time_calls(M, x, max(5, min(args.steps, 30)), flush)
+        rec = {"metric": METRIC, "workload_uuid": wl.uuid, "T": wl.T, "local_expert_offset": wl.offset,
+               "unit": "µs", "higher_is_better": False, "fp8_peak_source": FP8_PEAK_SOURCE}
+        rec.update(roofline_record(f, wl.T, us, pk, fp8_peak))
+        rec["status"] = M.device_status(device)
+        print(json.dumps(rec), flush=True)
 
 
 # ----------------------------------------------------------------------------- main
@@ -297,12 +350,17 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-sweeps", action="store_true")
     ap.add_argument("--cpu-experts", type=int, default=8)
+    ap.add_argument("--workloads", default=None, metavar="FILE",
+                    help="replay a flashinfer-bench workload file (jsonl): one JSON line per workload")
+    ap.add_argument("--blob-root", default=None, help="directory the workload file's blob paths are relative to")
     ap.add_argument("--case", default=None, metavar="T:E",
                     help="profiling case: W + K untimed layer calls at T tokens with E local experts "
                          "(seeded inputs, weights generated on the device); prints a status line only")
     args = ap.parse_args()
     if args.case:
         return profile_case(args)
+    if args.workloads:
+        return replay(args)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
