@@ -290,6 +290,23 @@ def sweep(device, steps, peaks_):
         stage_ms, calls = timer.read(reset=True)
         rec = {"workload": name, "T": T}
         rec.update(roofline_record(f, T, us, peaks_, fp8_peak))
+        if T <= 1024:
+            # the same call replayed from a CUDA graph (fixed shape: the serving decode mode)
+            g = M.GraphRunner(**x)
+            for _ in range(3):
+                g.replay()
+            gt = []
+            for _ in range(n):
+                flush.zero_()
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s.record()
+                g.replay()
+                e.record()
+                e.synchronize()
+                gt.append(s.elapsed_time(e) * 1e3)
+            gt.sort()
+            rec["graph_us"] = round(gt[len(gt) // 2], 1)
+            del g
         rec["stage_us"] = {k: round(v * 1e3 / calls, 1) for k, v in zip(("route", "gemm1", "gemm2"), stage_ms)}
         out.append(rec)
         del x

@@ -29,7 +29,7 @@ NHB = H // 128
 NIB = I // 128
 NG1B = 2 * I // 128
 
-__all__ = ["run", "kernel", "route", "device_status", "MoEArgumentError", "Workspace"]
+__all__ = ["run", "kernel", "route", "device_status", "MoEArgumentError", "Workspace", "GraphRunner"]
 
 
 class MoEArgumentError(AssertionError, ValueError):
@@ -160,6 +160,53 @@ def run(routing_logits: torch.Tensor, routing_bias: torch.Tensor, hidden_states:
 
 
 kernel = run
+
+
+class GraphRunner:
+    """One layer call captured in a CUDA graph, for callers that replay a fixed shape (decode
+    steps at a given batch size; the reference replays graphs the same way,
+    solution/python/kernel.py:1068-1089).
+
+    The arguments are those of :func:`run`; their tensors become the graph's static inputs (new
+    values are copied into them before :meth:`replay`).  The runner owns its workspace and its
+    output tensor, so later calls of :func:`run` with other sizes cannot move memory the graph
+    points at.  The first, eager call outside the graph sets up the tensor maps, the kernels'
+    attributes and the workspace's counters; the captured launches keep their programmatic
+    dependent-launch edges.
+    """
+
+    def __init__(self, routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
+                 gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_expert_offset,
+                 routed_scaling_factor):
+        T, E, dev = _validate(routing_logits, routing_bias, hidden_states, hidden_states_scale,
+                              gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale)
+        _check(T > 0, "an empty batch needs no graph")
+        self.inputs = dict(routing_logits=routing_logits, routing_bias=routing_bias,
+                           hidden_states=hidden_states, hidden_states_scale=hidden_states_scale)
+        self.out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+        n = int(_native.lib().moe_b200_workspace_size(T, E))
+        self.workspace = torch.zeros(n, dtype=torch.uint8, device=dev)   # zeroed = initialised
+        self._a = _args(T, E, routing_logits, routing_bias, hidden_states, hidden_states_scale,
+                        gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale,
+                        local_expert_offset, routed_scaling_factor, self.out)
+        self._keep = (gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale)
+        self._launch(torch.cuda.current_stream(dev).cuda_stream)     # eager set-up call
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self._launch(torch.cuda.current_stream(dev).cuda_stream)
+
+    def _launch(self, stream):
+        rc = _native.lib().moe_b200_forward(ctypes.byref(self._a), self.workspace.data_ptr(),
+                                            self.workspace.numel(), stream)
+        if rc != _native.OK:
+            raise RuntimeError(f"moe_b200_forward failed ({rc}): {_native.last_error()}")
+
+    def replay(self) -> torch.Tensor:
+        """Runs the captured call on the current values of the static inputs; returns the
+        runner's output tensor (overwritten by the next replay)."""
+        self.graph.replay()
+        return self.out
 
 
 @torch.no_grad()
