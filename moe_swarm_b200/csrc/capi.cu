@@ -121,8 +121,6 @@ moe::RouteArgs make_route_args(const moe_b200_args* a, uint8_t* ws, const moe::L
   r.offset = a->local_expert_offset;
   r.rsf = a->routed_scaling_factor;
   r.nchunks = L.nchunks;
-  r.num_sms = sms;
-  r.r_split = static_cast<int>(L.r_max < (size_t)moe::kRSplit ? L.r_max : (size_t)moe::kRSplit);
   r.r_pad = L.r_pad;
   r.plan = reinterpret_cast<moe::Plan*>(ws + L.plan);
   r.route_done = reinterpret_cast<int*>(ws + L.route_done);
@@ -137,10 +135,7 @@ moe::RouteArgs make_route_args(const moe_b200_args* a, uint8_t* ws, const moe::L
   r.e_count = reinterpret_cast<int*>(ws + L.e_count);
   r.e_start = reinterpret_cast<int*>(ws + L.e_start);
   r.e_mt_start = reinterpret_cast<int*>(ws + L.e_mt_start);
-  r.e_u1 = reinterpret_cast<int*>(ws + L.e_u1);
-  r.e_u2 = reinterpret_cast<int*>(ws + L.e_u2);
   r.e_tt = reinterpret_cast<int*>(ws + L.e_tt);
-  r.e_m64 = reinterpret_cast<int*>(ws + L.e_m64);
   r.row_token = reinterpret_cast<int*>(ws + L.row_token);
   r.row_weight = reinterpret_cast<float*>(ws + L.row_weight);
   r.a_perm = ws + L.a_perm;
@@ -275,7 +270,6 @@ moe::TileArgs tile_args(const moe_b200_args* a, uint8_t* ws, const moe::Layout& 
   s.tok_nloc = reinterpret_cast<const int*>(ws + L.tok_nloc);
   s.tok_rows = reinterpret_cast<const int*>(ws + L.tok_rows);
   s.part2 = reinterpret_cast<float*>(ws + L.part2);
-  s.cnt2 = reinterpret_cast<int*>(ws + L.cnt2);
   s.out = a->output;
   s.status = reinterpret_cast<int*>(ws + L.status);
   return s;

@@ -16,7 +16,7 @@ struct RouteArgs {
   uint16_t* out;
   int T, E, offset;
   float rsf;
-  int nchunks, num_sms, r_split;
+  int nchunks;
   size_t r_pad;
   Plan* plan;
   int* route_done;
@@ -31,10 +31,7 @@ struct RouteArgs {
   int* e_count;
   int* e_start;
   int* e_mt_start;
-  int* e_u1;
-  int* e_u2;
   int* e_tt;
-  int* e_m64;
   int* row_token;
   float* row_weight;
   uint8_t* a_perm;
@@ -65,7 +62,6 @@ struct TileArgs {
   const int* tok_nloc;
   const int* tok_rows;
   float* part2;
-  int* cnt2;
   uint16_t* out;
   int* status;
   unsigned long long* trace;   // [kMaxSms][kTraceSlots] of this kernel (written by MOE_TRACE builds)

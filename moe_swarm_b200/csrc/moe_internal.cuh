@@ -24,12 +24,9 @@ constexpr int kRouteWarps = 8;    // routing / scatter CTAs: one token per warp
 constexpr int kRouteThreads = kRouteWarps * 32;
 constexpr int kTok = 32;          // token tile (MMA N) of the streaming kernels
 constexpr int kMaxSms = 256;      // partial-slot capacity of the stream-K fixup (2 per CTA)
-constexpr int kStreamMaxT = 512;
+constexpr int kStreamMaxT = 512;  // T above which the wide (token-major) kernels run
 constexpr int kTraceSlots = 16;   // per-CTA counters of a traced build (MOE_TRACE)
-constexpr int kTraceKernels = 4;  // stream GEMM1, stream GEMM2, wide GEMM1, wide GEMM2  // T above which the wide (token-major) kernels run
-constexpr int kRSplit = 256;      // split-K is considered only when rows <= kRSplit
-constexpr int kS1Max = 14;        // GEMM1 split factors: divisors of 56 up to 14
-constexpr int kS2Max = 8;         // GEMM2 split factors: divisors of 16 up to 8
+constexpr int kTraceKernels = 4;  // stream GEMM1, stream GEMM2, wide GEMM1, wide GEMM2
 
 // Device status codes (first one wins).
 enum : int {
@@ -43,12 +40,10 @@ enum : int {
 
 // Written by the routing scan, read by the GEMM kernels.
 struct Plan {
-  int T, E, rows, m_tiles;
-  int s1, kb1, units1;    // wide GEMM1 split factor, K-blocks per split, work units
-  int s2, kb2, units2;    // wide GEMM2
+  int T, E, rows;
+  int m_tiles;            // 128-row token tiles (wide kernels)
   int tt;                 // 32-row token tiles (streaming kernels)
-  int m64;                // 64-row token tiles
-  int pad[4];
+  int pad[3];
 };
 
 struct Layout {
@@ -58,12 +53,12 @@ struct Layout {
   size_t plan, route_done, status;
   size_t topk_idx, topk_w, tok_nloc, tok_le, tok_lw, tok_rows;
   size_t chunk_hist, chunk_base;
-  size_t e_count, e_start, e_mt_start, e_u1, e_u2, e_tt, e_m64;
+  size_t e_count, e_start, e_mt_start, e_tt;
   size_t sk_part, sk_cnt, trace;
   size_t row_token, row_weight;
   size_t a_perm, sa_perm;
   size_t c_hi, c_lo, c_scale;
-  size_t part1, cnt1, part2, cnt2;
+  size_t part2;
   size_t counters_begin, counters_end;   // region zeroed by workspace_init
   size_t total;
 };
@@ -81,7 +76,6 @@ inline bool compute_layout(int T, int E, Layout* L) {
   l.r_max = tt * per_tok;
   l.r_pad = align_up(l.r_max, 32);
   l.mt_max = (l.r_max + kBlk - 1) / kBlk + E;
-  const size_t r_split = l.r_max < (size_t)kRSplit ? l.r_max : (size_t)kRSplit;
   size_t o = 0;
   auto take = [&](size_t bytes) {
     size_t at = align_up(o, 1024);
@@ -93,8 +87,6 @@ inline bool compute_layout(int T, int E, Layout* L) {
   l.counters_begin = align_up(o, 1024);
   l.route_done = take(sizeof(int));
   l.status = take(sizeof(int));
-  l.cnt1 = take(l.mt_max * kNT1 * sizeof(int));
-  l.cnt2 = take(tt * kNT2 * 2 * sizeof(int));
   l.chunk_hist = take((size_t)(l.nchunks > 0 ? l.nchunks : 1) * E * sizeof(int));
   l.sk_cnt = take(((l.r_max + kTok - 1) / kTok + E) * kNT2 * sizeof(int));
   l.counters_end = align_up(o, 1024);
@@ -108,10 +100,7 @@ inline bool compute_layout(int T, int E, Layout* L) {
   l.e_count = take((size_t)E * sizeof(int));
   l.e_start = take((size_t)(E + 1) * sizeof(int));
   l.e_mt_start = take((size_t)(E + 1) * sizeof(int));
-  l.e_u1 = take((size_t)(E + 1) * sizeof(int));
-  l.e_u2 = take((size_t)(E + 1) * sizeof(int));
   l.e_tt = take((size_t)(E + 1) * sizeof(int));
-  l.e_m64 = take((size_t)(E + 1) * sizeof(int));
   l.row_token = take(l.r_pad * sizeof(int));
   l.row_weight = take(l.r_pad * sizeof(float));
   l.a_perm = take(l.r_pad * kH);
@@ -119,9 +108,7 @@ inline bool compute_layout(int T, int E, Layout* L) {
   l.c_hi = take(l.r_pad * kI);
   l.c_lo = take(l.r_pad * kI);
   l.c_scale = take((size_t)kKB2 * l.r_pad * sizeof(float));
-  l.part1 = take((size_t)kS1Max * r_split * kN1 * sizeof(float));
-  const size_t p2_rows = l.r_pad > (size_t)kS2Max * r_split ? l.r_pad : (size_t)kS2Max * r_split;
-  l.part2 = take(p2_rows * kH * sizeof(float));
+  l.part2 = take(l.r_pad * kH * sizeof(float));   // fp32 rows of tokens with > 1 local expert
   l.sk_part = take((size_t)2 * kMaxSms * 128 * 256 * sizeof(float));
   l.trace = take((size_t)kTraceKernels * kMaxSms * kTraceSlots * sizeof(unsigned long long));
   l.total = align_up(o, 1024);

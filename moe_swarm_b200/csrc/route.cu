@@ -273,25 +273,6 @@ __device__ void scatter_token(const RouteArgs& a, int t, int tl, int lane,
   }
 }
 
-__device__ __forceinline__ float split_efficiency(int units, int sms) {
-  const int waves = (units + sms - 1) / sms;
-  return static_cast<float>(units) / static_cast<float>(waves * sms);
-}
-
-// Picks the split factor with the best last-wave fill; smaller splits win near-ties.
-__device__ int choose_split(int base_units, int sms, const int* cands, int ncand) {
-  int best = cands[0];
-  float best_eff = split_efficiency(base_units * cands[0], sms);
-  for (int i = 1; i < ncand; ++i) {
-    const float e = split_efficiency(base_units * cands[i], sms);
-    if (e > best_eff + 0.03f) {
-      best_eff = e;
-      best = cands[i];
-    }
-  }
-  return best;
-}
-
 // Chunk counts -> expert segment starts, per-chunk bases, tile prefixes and the plan.
 // Run by one whole CTA (blockDim >= 256); zeroes the chunk counts for the next call.
 __device__ void scan_plan(const RouteArgs& a, int* s_tmp, int* s_start) {
@@ -307,66 +288,43 @@ __device__ void scan_plan(const RouteArgs& a, int* s_tmp, int* s_start) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) cnt += v[j];
     }
-  // inclusive scans over experts of rows and of 128-, 64- and 32-row tiles
+  // inclusive scans over experts of rows and of 128- and 32-row tiles
   int* s_cnt = s_tmp;
   int* s_mt = s_tmp + 256;
-  int* s_m64 = s_tmp + 512;
-  int* s_tt = s_tmp + 768;
+  int* s_tt = s_tmp + 512;
   if (tid < 256) {
     const bool on = tid < E;
     s_cnt[tid] = on ? cnt : 0;
     s_mt[tid] = on ? (cnt + kBlk - 1) / kBlk : 0;
-    s_m64[tid] = on ? (cnt + 63) / 64 : 0;
     s_tt[tid] = on ? (cnt + kTok - 1) / kTok : 0;
   }
   __syncthreads();
   for (int d = 1; d < 256; d <<= 1) {
-    int v0 = 0, v1 = 0, v2 = 0, v3 = 0;
+    int v0 = 0, v1 = 0, v3 = 0;
     if (tid < 256 && tid >= d) {
       v0 = s_cnt[tid - d];
       v1 = s_mt[tid - d];
-      v2 = s_m64[tid - d];
       v3 = s_tt[tid - d];
     }
     __syncthreads();
     if (tid < 256 && tid >= d) {
       s_cnt[tid] += v0;
       s_mt[tid] += v1;
-      s_m64[tid] += v2;
       s_tt[tid] += v3;
     }
     __syncthreads();
   }
   const int rows = s_cnt[255];
   const int mtiles = s_mt[255];
-  __shared__ int s_split[2];
   if (tid == 0) {
-    int s1 = 1, s2 = 1;
-    if (rows <= kRSplit && rows > 0) {
-      const int c1[] = {1, 2, 4, 7, 8, 14};
-      const int c2[] = {1, 2, 4, 8};
-      s1 = choose_split(mtiles * kNT1, a.num_sms, c1, 6);
-      s2 = choose_split(mtiles * kNT2, a.num_sms, c2, 4);
-    }
-    s_split[0] = s1;
-    s_split[1] = s2;
     Plan p{};
     p.T = a.T;
     p.E = E;
     p.rows = rows;
     p.m_tiles = mtiles;
-    p.s1 = s1;
-    p.kb1 = kKB1 / s1;
-    p.units1 = mtiles * kNT1 * s1;
-    p.s2 = s2;
-    p.kb2 = kKB2 / s2;
-    p.units2 = mtiles * kNT2 * s2;
     p.tt = s_tt[255];
-    p.m64 = s_m64[255];
     *a.plan = p;
   }
-  __syncthreads();
-  const int s1 = s_split[0], s2 = s_split[1];
   if (tid < E) {
     const int start = s_cnt[tid] - cnt;
     const int mt0 = s_mt[tid] - (cnt + kBlk - 1) / kBlk;
@@ -374,10 +332,7 @@ __device__ void scan_plan(const RouteArgs& a, int* s_tmp, int* s_start) {
     a.e_count[tid] = cnt;
     a.e_start[tid] = start;
     a.e_mt_start[tid] = mt0;
-    a.e_u1[tid] = mt0 * kNT1 * s1;
-    a.e_u2[tid] = mt0 * kNT2 * s2;
     a.e_tt[tid] = s_tt[tid] - (cnt + kTok - 1) / kTok;
-    a.e_m64[tid] = s_m64[tid] - (cnt + 63) / 64;
     int run = start;
     for (int c0 = 0; c0 < a.nchunks; c0 += 8) {
       int v[8];
@@ -397,10 +352,7 @@ __device__ void scan_plan(const RouteArgs& a, int* s_tmp, int* s_start) {
   if (tid == 0) {
     a.e_start[E] = rows;
     a.e_mt_start[E] = mtiles;
-    a.e_u1[E] = mtiles * kNT1 * s1;
-    a.e_u2[E] = mtiles * kNT2 * s2;
     a.e_tt[E] = s_tt[255];
-    a.e_m64[E] = s_m64[255];
   }
   __syncthreads();
 }
@@ -517,7 +469,7 @@ __host__ __device__ constexpr NoAllocLayout noalloc_layout() {
   l.tok_nloc = na_align(l.tok_lw + kNoAllocMaxT * kTopK * sizeof(float));
   l.tok_rows = na_align(l.tok_nloc + kNoAllocMaxT * sizeof(int));
   l.tables = na_align(l.tok_rows + kNoAllocMaxT * kTopK * sizeof(int));
-  l.total = na_align(l.tables + 6 * (kEG + 1) * sizeof(int));
+  l.total = na_align(l.tables + 3 * (kEG + 1) * sizeof(int));
   return l;
 }
 static_assert(noalloc_layout().total <= kNoAllocScratchBytes, "no-alloc scratch too small");
@@ -585,7 +537,6 @@ extern "C" MOE_B200_API int moe_b200_route_noalloc(const moe_b200_args* args, in
   r.offset = args->local_expert_offset;
   r.rsf = args->routed_scaling_factor;
   r.nchunks = (T + kChunk - 1) / kChunk;
-  r.num_sms = 148;
   r.r_pad = 0;
   r.plan = reinterpret_cast<Plan*>(sp + L.plan);
   r.topk_idx = topk_idx;
@@ -600,10 +551,7 @@ extern "C" MOE_B200_API int moe_b200_route_noalloc(const moe_b200_args* args, in
   r.e_count = expert_count;
   r.e_start = tab;
   r.e_mt_start = tab + (kEG + 1);
-  r.e_u1 = tab + 2 * (kEG + 1);
-  r.e_u2 = tab + 3 * (kEG + 1);
-  r.e_tt = tab + 4 * (kEG + 1);
-  r.e_m64 = tab + 5 * (kEG + 1);
+  r.e_tt = tab + 2 * (kEG + 1);
   r.row_token = row_token;
   r.row_weight = row_weight;
   // no activation copy and no output rows: routing and permutation metadata only
