@@ -88,7 +88,7 @@ typedef struct moe_b200_args {
  * for the T passed to moe_b200_workspace_layout.
  */
 typedef struct moe_b200_layout {
-  size_t plan;        /* int32[16]: T, E_local, rows, m_tiles, s1, kb1, units1, s2, kb2, units2 */
+  size_t plan;        /* int32[8]: T, E_local, rows, 128-row token tiles, 32-row token tiles */
   size_t topk_idx;    /* int32 [T, 8]: selected global experts, ascending per token */
   size_t topk_w;      /* f32   [T, 8]: their combine weights (bias-free, normalised, x rsf) */
   size_t tok_nloc;    /* int32 [T]: number of local experts each token selected */
@@ -130,6 +130,19 @@ MOE_B200_API int moe_b200_workspace_init(void* workspace, size_t workspace_bytes
  */
 MOE_B200_API int moe_b200_forward(const moe_b200_args* args, void* workspace, size_t workspace_bytes,
                      void* stream);
+
+/*
+ * The layer with the routing given by the caller instead of computed from logits: token t's
+ * experts are topk_idx[t, 0..7] (global ids, distinct per token) with combine weights
+ * topk_w[t, 0..7] (routed_scaling_factor already applied); routing_logits, routing_bias and
+ * routed_scaling_factor of `args` are not read.  Otherwise as moe_b200_forward.  For
+ * token-dispatch expert parallelism, where a rank receives tokens routed elsewhere.  It
+ * replaces the routing half of the reference's kernel(...) (solution/python/kernel.py:137-213);
+ * the rest of the call is the same.
+ */
+MOE_B200_API int moe_b200_forward_routed(const moe_b200_args* args, const int32_t* topk_idx,
+                                         const float* topk_w, void* workspace, size_t workspace_bytes,
+                                         void* stream);
 
 /*
  * Routing and permutation only (the reference's _route_kernel + _pf_permute_kernel,

@@ -29,7 +29,8 @@ NHB = H // 128
 NIB = I // 128
 NG1B = 2 * I // 128
 
-__all__ = ["run", "kernel", "route", "device_status", "MoEArgumentError", "Workspace", "GraphRunner"]
+__all__ = ["run", "kernel", "run_routed", "route", "device_status", "MoEArgumentError", "Workspace",
+           "GraphRunner"]
 
 
 class MoEArgumentError(AssertionError, ValueError):
@@ -160,6 +161,46 @@ def run(routing_logits: torch.Tensor, routing_bias: torch.Tensor, hidden_states:
 
 
 kernel = run
+
+
+@torch.no_grad()
+def run_routed(topk_idx: torch.Tensor, topk_w: torch.Tensor, hidden_states: torch.Tensor,
+               hidden_states_scale: torch.Tensor, gemm1_weights: torch.Tensor,
+               gemm1_weights_scale: torch.Tensor, gemm2_weights: torch.Tensor,
+               gemm2_weights_scale: torch.Tensor, local_expert_offset: int, *,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    """The layer with the routing given instead of computed: token t's experts are
+    ``topk_idx[t]`` (int32 ``[T, 8]`` global ids, distinct per token) weighted by ``topk_w[t]``
+    (float32 ``[T, 8]``, routed scaling factor already applied).  Only the local experts
+    ``[local_expert_offset, local_expert_offset + E_local)`` contribute; returns bf16 ``[T, 7168]``.
+    Used by token-dispatch expert parallelism (``ep.ExpertParallelMoE.forward_dispatch``)."""
+    T = hidden_states.shape[0]
+    dummy_logits = torch.empty((T, E_GLOBAL), dtype=torch.float32, device=hidden_states.device)
+    dummy_bias = torch.empty(E_GLOBAL, dtype=torch.bfloat16, device=hidden_states.device)
+    T, E, dev = _validate(dummy_logits, dummy_bias, hidden_states, hidden_states_scale, gemm1_weights,
+                          gemm1_weights_scale, gemm2_weights, gemm2_weights_scale)
+    _check(tuple(topk_idx.shape) == (T, 8) and topk_idx.dtype == torch.int32 and topk_idx.is_contiguous()
+           and topk_idx.device == dev, "topk_idx must be a contiguous int32 [T, 8] tensor on the device")
+    _check(tuple(topk_w.shape) == (T, 8) and topk_w.dtype == torch.float32 and topk_w.is_contiguous()
+           and topk_w.device == dev, "topk_w must be a contiguous float32 [T, 8] tensor on the device")
+    if out is None:
+        out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    else:
+        _check(out.dtype == torch.bfloat16 and tuple(out.shape) == (T, H) and out.is_contiguous()
+               and out.device == dev, "out must be a contiguous bf16 [T, 7168] tensor on the device")
+    if T == 0:
+        return out
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    buf = _workspace(dev).get(T, E, stream)
+    a = _args(T, E, dummy_logits, dummy_bias, hidden_states, hidden_states_scale, gemm1_weights,
+              gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_expert_offset, 1.0, out)
+    a.routing_logits = None
+    a.routing_bias = None
+    rc = _native.lib().moe_b200_forward_routed(ctypes.byref(a), topk_idx.data_ptr(), topk_w.data_ptr(),
+                                               buf.data_ptr(), buf.numel(), stream)
+    if rc != _native.OK:
+        raise RuntimeError(f"moe_b200_forward_routed failed ({rc}): {_native.last_error()}")
+    return out
 
 
 class GraphRunner:

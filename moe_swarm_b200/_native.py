@@ -25,6 +25,7 @@ EXPORTED = (
     "moe_b200_workspace_layout",
     "moe_b200_workspace_init",
     "moe_b200_forward",
+    "moe_b200_forward_routed",
     "moe_b200_route",
     "moe_b200_device_status",
     "moe_b200_last_error",
@@ -83,6 +84,8 @@ def lib() -> ctypes.CDLL:
     l.moe_b200_workspace_init.restype = ctypes.c_int
     l.moe_b200_forward.argtypes = [ctypes.POINTER(MoeArgs), vp, sz, vp]
     l.moe_b200_forward.restype = ctypes.c_int
+    l.moe_b200_forward_routed.argtypes = [ctypes.POINTER(MoeArgs), vp, vp, vp, sz, vp]
+    l.moe_b200_forward_routed.restype = ctypes.c_int
     l.moe_b200_route.argtypes = [ctypes.POINTER(MoeArgs), vp, sz, vp]
     l.moe_b200_route.restype = ctypes.c_int
     l.moe_b200_device_status.argtypes = [vp, sz, i32, i32, vp, i32]

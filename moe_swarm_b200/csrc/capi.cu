@@ -92,19 +92,20 @@ DeviceInfo& device_info(int dev) {
   return d;
 }
 
-int check_args(const moe_b200_args* a) {
+// pre_routed: moe_b200_forward_routed, whose routing_logits / routing_bias are not read.
+int check_args(const moe_b200_args* a, bool pre_routed) {
   if (!a) return fail(MOE_B200_ERR_ARG, "null args");
   if (a->num_tokens < 0) return fail(MOE_B200_ERR_ARG, "num_tokens < 0");
   if (a->num_local_experts < 1 || a->num_local_experts > moe::kEG)
     return fail(MOE_B200_ERR_ARG, "num_local_experts must be in [1, 256]");
   if (a->num_tokens == 0) return MOE_B200_OK;
-  if (!a->routing_logits || !a->routing_bias || !a->hidden_states || !a->hidden_states_scale ||
+  if ((!pre_routed && (!a->routing_logits || !a->routing_bias)) || !a->hidden_states || !a->hidden_states_scale ||
       !a->gemm1_weights || !a->gemm1_weights_scale || !a->gemm2_weights || !a->gemm2_weights_scale ||
       !a->output)
     return fail(MOE_B200_ERR_ARG, "null tensor pointer");
   auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
   if (!al16(a->gemm1_weights) || !al16(a->gemm2_weights) || !al16(a->hidden_states) ||
-      !al16(a->routing_logits) || !al16(a->output))
+      (!pre_routed && !al16(a->routing_logits)) || !al16(a->output))
     return fail(MOE_B200_ERR_ARG, "weights, hidden states, logits and output must be 16-byte aligned");
   return MOE_B200_OK;
 }
@@ -143,8 +144,9 @@ moe::RouteArgs make_route_args(const moe_b200_args* a, uint8_t* ws, const moe::L
   return r;
 }
 
-int prepare(const moe_b200_args* a, void* workspace, size_t ws_bytes, moe::Layout* L, int* dev_out) {
-  int rc = check_args(a);
+int prepare(const moe_b200_args* a, void* workspace, size_t ws_bytes, moe::Layout* L, int* dev_out,
+            bool pre_routed = false) {
+  int rc = check_args(a, pre_routed);
   if (rc) return rc;
   if (!moe::compute_layout(a->num_tokens, a->num_local_experts, L))
     return fail(MOE_B200_ERR_ARG, "bad sizes");
@@ -163,9 +165,11 @@ int prepare(const moe_b200_args* a, void* workspace, size_t ws_bytes, moe::Layou
 // expert (moe_b200_route); the full layer leaves them to the combine kernel instead, which
 // runs on every SM rather than on the single routing CTA of small batches.
 int launch_route(const moe_b200_args* a, uint8_t* ws, const moe::Layout& L, int sms, cudaStream_t st,
-                 int* launches, bool zero_rows) {
+                 int* launches, bool zero_rows, const int32_t* pre_idx = nullptr, const float* pre_w = nullptr) {
   moe::RouteArgs r = make_route_args(a, ws, L, sms);
   if (!zero_rows) r.out = nullptr;
+  r.pre_idx = pre_idx;
+  r.pre_w = pre_w;
   cudaError_t e = moe::route_launch(r, st, launches);
   if (e != cudaSuccess) return cuda_fail(e, "route launch");
   return MOE_B200_OK;
@@ -276,11 +280,11 @@ moe::TileArgs tile_args(const moe_b200_args* a, uint8_t* ws, const moe::Layout& 
 }
 
 int forward_impl(const moe_b200_args* a, void* workspace, size_t ws_bytes, void* stream,
-                 moe_b200_timer* timer) {
+                 moe_b200_timer* timer, const int32_t* pre_idx = nullptr, const float* pre_w = nullptr) {
   g_last_launches = 0;
   moe::Layout L;
   int dev = 0;
-  int rc = prepare(a, workspace, ws_bytes, &L, &dev);
+  int rc = prepare(a, workspace, ws_bytes, &L, &dev, pre_idx != nullptr);
   if (rc) return rc;
   if (a->num_tokens == 0) return MOE_B200_OK;
   DeviceInfo& di = device_info(dev);
@@ -307,7 +311,7 @@ int forward_impl(const moe_b200_args* a, void* workspace, size_t ws_bytes, void*
     cudaEventRecord(ev[0], st);
   }
   int launches = 0;
-  rc = launch_route(a, ws, L, di.sms, st, &launches, false);
+  rc = launch_route(a, ws, L, di.sms, st, &launches, false, pre_idx, pre_w);
   if (rc) return rc;
   if (ev) cudaEventRecord(ev[1], st);
 
@@ -389,6 +393,12 @@ extern "C" {
 
 int moe_b200_forward(const moe_b200_args* a, void* workspace, size_t ws_bytes, void* stream) {
   return forward_impl(a, workspace, ws_bytes, stream, nullptr);
+}
+
+int moe_b200_forward_routed(const moe_b200_args* a, const int32_t* topk_idx, const float* topk_w,
+                            void* workspace, size_t ws_bytes, void* stream) {
+  if (a && a->num_tokens > 0 && (!topk_idx || !topk_w)) return fail(MOE_B200_ERR_ARG, "null topk_idx / topk_w");
+  return forward_impl(a, workspace, ws_bytes, stream, nullptr, topk_idx, topk_w);
 }
 
 moe_b200_timer* moe_b200_timer_create(void) { return new moe_b200_timer(); }

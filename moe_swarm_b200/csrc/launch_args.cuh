@@ -16,6 +16,9 @@ struct RouteArgs {
   uint16_t* out;
   int T, E, offset;
   float rsf;
+  // pre-routed calls (moe_b200_forward_routed): the caller's picks replace the routing
+  const int* pre_idx;     // [T, 8] global expert ids, null for routed calls
+  const float* pre_w;     // [T, 8] combine weights
   int nchunks;
   size_t r_pad;
   Plan* plan;

@@ -201,6 +201,37 @@ __device__ void route_token(const RouteArgs& a, const float* s_bias, int t, int 
   if (lane == 0) a.tok_nloc[t] = nloc;
 }
 
+// Pre-routed token t (moe_b200_forward_routed): the caller's 8 picks (global expert id and
+// combine weight) take the place of the routing.  Lanes 0..7 hold the picks; the local ones are
+// written in ascending expert order -- the row order of the permutation and the order of the
+// combine's sum -- and counted in the token's chunk histogram.  A token's ids must be distinct.
+__device__ void pick_token(const RouteArgs& a, int t, int lane) {
+  int ge = -1;
+  float w = 0.f;
+  if (lane < kTopK) {
+    ge = __ldg(a.pre_idx + static_cast<size_t>(t) * kTopK + lane);
+    w = __ldg(a.pre_w + static_cast<size_t>(t) * kTopK + lane);
+    a.topk_idx[static_cast<size_t>(t) * kTopK + lane] = ge;
+    a.topk_w[static_cast<size_t>(t) * kTopK + lane] = w;
+  }
+  const bool local = lane < kTopK && ge >= a.offset && ge < a.offset + a.E;
+  int rank = 0;
+#pragma unroll
+  for (int j = 0; j < kTopK; ++j) {
+    const int gj = __shfl_sync(0xffffffffu, ge, j);
+    const int lj = __shfl_sync(0xffffffffu, local ? 1 : 0, j);
+    if (lj && (gj < ge || (gj == ge && j < lane))) ++rank;
+  }
+  if (local) {
+    const int le = ge - a.offset;
+    a.tok_le[static_cast<size_t>(t) * kTopK + rank] = le;
+    a.tok_lw[static_cast<size_t>(t) * kTopK + rank] = w;
+    atomicAdd(a.chunk_hist + static_cast<size_t>(t / kChunk) * a.E + le, 1);
+  }
+  const int nloc = __popc(__ballot_sync(0xffffffffu, local));
+  if (lane == 0) a.tok_nloc[t] = nloc;
+}
+
 // Per-expert token bitmask of chunk c, built by the whole CTA from the tokens' pick lists.
 __device__ void build_chunk_masks(const RouteArgs& a, int c, uint32_t (*s_mask)[kChunk / 32]) {
   for (int i = threadIdx.x; i < a.E * (kChunk / 32); i += blockDim.x) (&s_mask[0][0])[i] = 0;
@@ -363,10 +394,14 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
   __shared__ int s_start[kEG];
   __shared__ int s_last;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  for (int i = tid; i < kEG; i += blockDim.x) s_bias[i] = bf16_bits_to_float(a.bias[i]);
+  if (!a.pre_idx)   // pre-routed calls have no logits or bias
+    for (int i = tid; i < kEG; i += blockDim.x) s_bias[i] = bf16_bits_to_float(a.bias[i]);
   __syncthreads();
   const int t = blockIdx.x * kRouteWarps + warp;
-  if (t < a.T) route_token(a, s_bias, t, lane);
+  if (t < a.T) {
+    if (a.pre_idx) pick_token(a, t, lane);
+    else route_token(a, s_bias, t, lane);
+  }
   __threadfence();
   __syncthreads();
   if (tid == 0) {
@@ -408,9 +443,13 @@ __device__ __forceinline__ void route_small_body(const RouteArgs& a) {
   __shared__ int s_start[kEG];
   __shared__ int s_base[kEG];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  for (int i = tid; i < kEG; i += blockDim.x) s_bias[i] = bf16_bits_to_float(a.bias[i]);
+  if (!a.pre_idx)   // pre-routed calls have no logits or bias
+    for (int i = tid; i < kEG; i += blockDim.x) s_bias[i] = bf16_bits_to_float(a.bias[i]);
   __syncthreads();
-  for (int t = warp; t < a.T; t += kRouteSmallThreads / 32) route_token(a, s_bias, t, lane);
+  for (int t = warp; t < a.T; t += kRouteSmallThreads / 32) {
+    if (a.pre_idx) pick_token(a, t, lane);
+    else route_token(a, s_bias, t, lane);
+  }
   __syncthreads();
   scan_plan(a, s_tmp, s_start);
   for (int c = 0; c < a.nchunks; ++c) {

@@ -8,6 +8,11 @@ This module is that caller: rank r of N holds experts [r*256/N, (r+1)*256/N), hi
 and logits are replicated, and the bf16 partial outputs are combined over NCCL -- by
 reduce-scatter (rank r keeps token rows [r*T/N, (r+1)*T/N), the input layout of a following
 sequence-sharded layer) or by all-reduce (every rank keeps all rows).
+
+`forward_dispatch` is the token-dispatch form a deployment uses when each rank owns its own
+tokens: a rank routes its tokens, sends each one only to the ranks holding its experts
+(all-to-all), computes the tokens it received with the pre-routed layer on its experts, and
+sends the partial rows back (all-to-all), where each token's rows are summed in rank order.
 """
 
 from __future__ import annotations
@@ -51,14 +56,26 @@ def row_split(T: int, world: int):
     return [(r * n, (r + 1) * n) for r in range(world)]
 
 
+def _default_route(routing_logits, routing_bias, routed_scaling_factor, like):
+    """Device routing of a rank's own tokens: (topk_idx int32 [T, 8] global ids, topk_w f32)."""
+    from . import route
+    r = route(routing_logits, routing_bias, like["hidden_states"], like["hidden_states_scale"],
+              like["gemm1_weights"], like["gemm1_weights_scale"], like["gemm2_weights"],
+              like["gemm2_weights_scale"], 0, routed_scaling_factor)
+    return r["topk_idx"].clone(), r["topk_w"].clone()   # copies: route() returns workspace views
+
+
 class ExpertParallelMoE:
     """The layer on one rank of an expert-parallel group.
 
     ``local`` computes this rank's partial output from the layer's ten arguments (by default
-    :func:`moe_swarm_b200.run`); the group's collective combines the partials.
+    :func:`moe_swarm_b200.run`); the group's collective combines the partials.  For
+    :meth:`forward_dispatch`, ``route_fn(logits, bias, rsf, like)`` gives a rank's routing and
+    ``local_routed`` the pre-routed partial output (by default the device routing and
+    :func:`moe_swarm_b200.run_routed`).
     """
 
-    def __init__(self, group=None, local=None):
+    def __init__(self, group=None, local=None, route_fn=None, local_routed=None):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -66,6 +83,10 @@ class ExpertParallelMoE:
         if local is None:
             from . import run as local
         self.local = local
+        if local_routed is None:
+            from . import run_routed as local_routed
+        self.local_routed = local_routed
+        self.route_fn = route_fn or _default_route
 
     def partial(self, routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
                 gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, routed_scaling_factor):
@@ -93,3 +114,51 @@ class ExpertParallelMoE:
             out = torch.empty((hi - lo,) + tuple(part.shape[1:]), dtype=part.dtype, device=part.device)
         dist.reduce_scatter_tensor(out, part, group=self.group)
         return out
+
+    def _exchange(self, send: torch.Tensor, send_counts, recv_counts) -> torch.Tensor:
+        """all_to_all of rows: send's rows grouped by destination rank in rank order."""
+        out = torch.empty((int(sum(recv_counts)),) + tuple(send.shape[1:]), dtype=send.dtype, device=send.device)
+        dist.all_to_all_single(out, send, output_split_sizes=list(recv_counts),
+                               input_split_sizes=list(send_counts), group=self.group)
+        return out
+
+    def forward_dispatch(self, routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
+                         gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, routed_scaling_factor):
+        """Token-dispatch expert parallelism over this rank's own T tokens; returns their bf16
+        [T, 7168] output rows.  Every rank's weights are its shard of the 256 experts."""
+        if gemm1_weights.shape[0] != self.shard.experts:
+            raise ValueError(f"rank {self.rank} holds {self.shard.experts} experts, got weights for "
+                             f"{gemm1_weights.shape[0]}")
+        like = dict(hidden_states=hidden_states, hidden_states_scale=hidden_states_scale,
+                    gemm1_weights=gemm1_weights, gemm1_weights_scale=gemm1_weights_scale,
+                    gemm2_weights=gemm2_weights, gemm2_weights_scale=gemm2_weights_scale)
+        topk_idx, topk_w = self.route_fn(routing_logits, routing_bias, routed_scaling_factor, like)
+        T = hidden_states.shape[0]
+        dev = hidden_states.device
+        # the ranks each token goes to: those holding at least one of its experts
+        owner = (topk_idx.long() // self.shard.experts).clamp(0, self.world - 1)
+        goes = torch.zeros((self.world, T), dtype=torch.bool, device=dev)
+        goes.scatter_(0, owner.t().contiguous(), torch.ones_like(owner.t(), dtype=torch.bool))
+        dest_tokens = [goes[d].nonzero().squeeze(1) for d in range(self.world)]   # ascending token ids
+        send_counts = torch.tensor([len(x) for x in dest_tokens], dtype=torch.int64, device=dev)
+        recv_counts = torch.empty_like(send_counts)
+        dist.all_to_all_single(recv_counts, send_counts, group=self.group)
+        sc, rc = send_counts.tolist(), recv_counts.tolist()
+        sel = torch.cat(dest_tokens)
+        hs_u8 = hidden_states.view(torch.uint8)
+        r_hidden = self._exchange(hs_u8.index_select(0, sel).contiguous(), sc, rc)
+        r_scale = self._exchange(hidden_states_scale.t().index_select(0, sel).contiguous(), sc, rc)
+        r_idx = self._exchange(topk_idx.index_select(0, sel).contiguous(), sc, rc)
+        r_w = self._exchange(topk_w.index_select(0, sel).contiguous(), sc, rc)
+        part = self.local_routed(r_idx, r_w, r_hidden.view(hidden_states.dtype), r_scale.t().contiguous(),
+                                 gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale,
+                                 self.shard.offset)
+        back = self._exchange(part.contiguous(), rc, sc)      # this rank's tokens, grouped by source rank
+        out = torch.zeros((T, back.shape[1]), dtype=torch.float32, device=dev)
+        start = 0
+        for d in range(self.world):                             # rank order: deterministic sum
+            n = sc[d]
+            if n:
+                out.index_add_(0, dest_tokens[d], back[start:start + n].float())
+            start += n
+        return out.to(torch.bfloat16)

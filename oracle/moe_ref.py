@@ -118,14 +118,12 @@ def expert_forward(A_e: torch.Tensor, W13_e: torch.Tensor, W2_e: torch.Tensor):
 
 
 @torch.no_grad()
-def run_fp32(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
-             gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_expert_offset,
-             routed_scaling_factor):
-    """The official layer output before the final bf16 cast, f32 [T, H]."""
-    T = routing_logits.shape[0]
+def _experts_fp32(A, topk_idx, weights, gemm1_weights, gemm1_weights_scale, gemm2_weights,
+                  gemm2_weights_scale, local_expert_offset):
+    """The official layer after routing (spec/reference_official.py:128-168): each local expert
+    in ascending order runs its routed tokens, weighted rows index_add_ed into f32 [T, H]."""
+    T = A.shape[0]
     E_local = gemm1_weights.shape[0]
-    A = dequant_tokens(hidden_states, hidden_states_scale)
-    topk_idx, weights = route(routing_logits, routing_bias, routed_scaling_factor)
     output = torch.zeros((T, H), dtype=torch.float32)
     local_start = int(local_expert_offset)
     for le in range(E_local):                                              # :134
@@ -142,6 +140,30 @@ def run_fp32(routing_logits, routing_bias, hidden_states, hidden_states_scale, g
         w_tok = weights.index_select(0, token_idx)[:, ge]
         output.index_add_(0, token_idx, O * w_tok.unsqueeze(1))            # :165-166
     return output
+
+
+def run_fp32(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
+             gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_expert_offset,
+             routed_scaling_factor):
+    """The official layer output before the final bf16 cast, f32 [T, H]."""
+    A = dequant_tokens(hidden_states, hidden_states_scale)
+    topk_idx, weights = route(routing_logits, routing_bias, routed_scaling_factor)
+    return _experts_fp32(A, topk_idx, weights, gemm1_weights, gemm1_weights_scale, gemm2_weights,
+                         gemm2_weights_scale, local_expert_offset)
+
+
+def run_routed(topk_idx, topk_w, hidden_states, hidden_states_scale, gemm1_weights, gemm1_weights_scale,
+               gemm2_weights, gemm2_weights_scale, local_expert_offset):
+    """The official layer with the routing given instead of computed -- token t's experts
+    ``topk_idx[t]`` weighted by ``topk_w[t]`` -- i.e. ``run`` from the point its routing is known
+    (spec/reference_official.py:128-168); the oracle of the pre-routed entry point.  bf16."""
+    T = hidden_states.shape[0]
+    A = dequant_tokens(hidden_states, hidden_states_scale)
+    idx = topk_idx.long()
+    dense = torch.zeros((T, E_GLOBAL), dtype=torch.float32)
+    dense.scatter_(1, idx, topk_w.float())
+    return _experts_fp32(A, idx, dense, gemm1_weights, gemm1_weights_scale, gemm2_weights,
+                         gemm2_weights_scale, local_expert_offset).to(torch.bfloat16)
 
 
 def run(*args, **kwargs):

@@ -113,3 +113,58 @@ def test_two_rank_nccl_matches_single_gpu(tmp_path):
     assert int(bad.sum()) <= 1e-3 * want.numel(), f"{int(bad.sum())} elements outside tolerance"
     assert float(err.max()) <= 5 * C.ATOL
     assert want.abs().max() > 0
+
+
+def _dispatch_rank_main(rank, world, port, out_dir):
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    from moe_swarm_b200 import ep
+    from moe_swarm_b200 import workload as W
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    device = torch.device("cuda", rank)
+    torch.cuda.set_device(device)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                            device_id=device)
+    try:
+        sh = ep.shard(rank, world)
+        x = _layer_inputs(device, sh.offset, sh.experts)
+        own = {k: v.to(device) for k, v in W.make_steered_activations(T, SEED + 1 + rank, 0, FAVOUR).items()}
+        layer = ep.ExpertParallelMoE()
+        out = layer.forward_dispatch(own["routing_logits"], own["routing_bias"], own["hidden_states"],
+                                     own["hidden_states_scale"], x["gemm1_weights"], x["gemm1_weights_scale"],
+                                     x["gemm2_weights"], x["gemm2_weights_scale"], 2.5)
+        torch.cuda.synchronize()
+        torch.save(out.cpu(), os.path.join(out_dir, f"dispatch{rank}.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_token_dispatch_matches_single_gpu(tmp_path):
+    """Token-dispatch EP (each rank routes its own tokens, all-to-all to the expert owners,
+    pre-routed layer, all-to-all back): every rank's rows match the single-GPU layer over all
+    256 experts for its tokens, within the bar of the broadcast test above."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    import moe_swarm_b200 as M
+    from moe_swarm_b200 import workload as W
+
+    mp.start_processes(_dispatch_rank_main, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True,
+                       start_method="spawn")
+    dev = torch.device("cuda", 0)
+    full = _layer_inputs(dev, 0, 256)
+    for rank in range(2):
+        got = torch.load(tmp_path / f"dispatch{rank}.pt").float()
+        own = {k: v.to(dev) for k, v in W.make_steered_activations(T, SEED + 1 + rank, 0, FAVOUR).items()}
+        want = M.run(**{**full, **own}, local_expert_offset=0, routed_scaling_factor=2.5).float().cpu()
+        err = (got - want).abs()
+        bad = err > C.ATOL + C.RTOL * want.abs()
+        assert int(bad.sum()) <= 1e-3 * want.numel(), f"rank {rank}: {int(bad.sum())} elements outside tolerance"
+        assert float(err.max()) <= 5 * C.ATOL
+        assert want.abs().max() > 0
