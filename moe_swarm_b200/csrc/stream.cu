@@ -9,17 +9,16 @@
 //       D1 = W13[X1 rows] . A^T,  D2 = W13[X2 rows] . A^T   (fp8 x fp8 -> fp32 TMEM)
 //       acc_i[r][c] += D_i[r][c] * s13[e, block_i, kb] * sa[token c, kb]   (exact fp32 scales)
 //     epilogue: C = silu(X2) * X1 per (feature r, token c); per-token amax over the tile's
-//     128 features; C stored as the e4m3 pair C ~= s*(hi + lo), hi = e4m3(C/s), lo =
-//     e4m3(C/s - hi), s = amax/448.  A tile
-//     that stream-K split over several CTAs is summed and finished by stream_fin1_kernel, a
-//     programmatic dependent of this kernel, so no CTA's range ends with a wait-free but
-//     latency-bound fixup and epilogue on the critical path.
+//     128 features; C stored as the e4m3 pair C ~= s*(hi + lo), hi = e4m3(C/s),
+//     lo = e4m3(C/s - hi), s = amax/448.  A tile that stream-K split over several CTAs is
+//     summed and finished by stream_fin1_kernel, a programmatic dependent of this kernel, so
+//     no CTA's range ends with a latency-bound fixup and epilogue on the critical path.
 //   MODE 2 (GEMM2): tile = (expert, 32-token tile, 128 output features nt); K = 16 blocks.
 //       D = W2 . C_hi^T + W2 . C_lo^T   (one accumulator: hi and lo share every scale)
 //       acc[r][c] += D[r][c] * s2[e, nt, kb] * sc[token c, kb]
-//     epilogue: out[t, f] = bf16(w * O) for a token with one local expert; otherwise the
-//     token's rows are summed in ascending expert order by the last contributing tile
-//     (per-(token, 128-feature) arrival counter) -- deterministic.
+//     epilogue: out[t, f] = bf16(w * O) for a token with one local expert; otherwise w * O
+//     goes to the token's fp32 partial row, summed in ascending expert order by the combine
+//     kernel (combine.cu) -- deterministic.  A split tile is finished by its last contributor.
 //
 // Work is split stream-K over the persistent CTAs (sched.cuh), so all SMs stream weights
 // even when routing activates a few experts.  CTA = 6 warps: warp 0 TMA producer, warp 1
