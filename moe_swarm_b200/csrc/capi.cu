@@ -22,7 +22,7 @@ cudaError_t wide_launch(int mode, int grid, cudaStream_t st, const CUtensorMap& 
                         const CUtensorMap& b, const TileArgs& g);
 cudaError_t stream_prepare();
 cudaError_t combine_launch(int T, int grid, cudaStream_t st, const int* tok_nloc, const int* tok_rows,
-                           const float* part2, uint16_t* out);
+                           const float* part2, uint16_t* out, unsigned long long* trace);
 cudaError_t stream_launch(int mode, int grid, cudaStream_t st, const CUtensorMap& w, const CUtensorMap& t,
                           const CUtensorMap& t2, const TileArgs& g);
 cudaError_t stream_fin_launch(int G, cudaStream_t st, const TileArgs& g);
@@ -141,6 +141,7 @@ moe::RouteArgs make_route_args(const moe_b200_args* a, uint8_t* ws, const moe::L
   r.row_weight = reinterpret_cast<float*>(ws + L.row_weight);
   r.a_perm = ws + L.a_perm;
   r.sa_perm = reinterpret_cast<float*>(ws + L.sa_perm);
+  r.trace = reinterpret_cast<unsigned long long*>(ws + L.trace) + 4 * (size_t)moe::kMaxSms * moe::kTraceSlots;
   return r;
 }
 
@@ -251,7 +252,9 @@ int launch_combine(const moe_b200_args* a, uint8_t* ws, const moe::Layout& L, in
   const int grid = T < 8 * sms ? T : 8 * sms;
   cudaError_t e = moe::combine_launch(T, grid, st, reinterpret_cast<const int*>(ws + L.tok_nloc),
                                       reinterpret_cast<const int*>(ws + L.tok_rows),
-                                      reinterpret_cast<const float*>(ws + L.part2), a->output);
+                                      reinterpret_cast<const float*>(ws + L.part2), a->output,
+                                      reinterpret_cast<unsigned long long*>(ws + L.trace) +
+                                          7 * (size_t)moe::kMaxSms * moe::kTraceSlots);
   if (e != cudaSuccess) return cuda_fail(e, "combine launch");
   ++*launches;
   return MOE_B200_OK;
@@ -335,7 +338,9 @@ int forward_impl(const moe_b200_args* a, void* workspace, size_t ws_bytes, void*
     cudaError_t e = moe::stream_launch(1, grid, st, mW13s, mTok, mTok, s1);
     if (e != cudaSuccess) return cuda_fail(e, "stream gemm1 launch");
     ++launches;
-    e = moe::stream_fin_launch(grid, st, s1);
+    moe::TileArgs s1f = s1;
+    s1f.trace = trace + 6 * (size_t)moe::kMaxSms * moe::kTraceSlots;
+    e = moe::stream_fin_launch(grid, st, s1f);
     if (e != cudaSuccess) return cuda_fail(e, "stream gemm1 finish launch");
     ++launches;
     if (ev) cudaEventRecord(ev[2], st);

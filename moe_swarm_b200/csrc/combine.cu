@@ -15,8 +15,11 @@ namespace moe {
 constexpr int kCombineThreads = 256;
 
 __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const int* tok_nloc, const int* tok_rows,
-                                                                  const float* part2, uint16_t* out, int T) {
+                                                                  const float* part2, uint16_t* out, int T,
+                                                                  unsigned long long* trace) {
+  MOE_TRACE_CTA(trace, 0);
   pdl_wait();   // the partial rows come from GEMM2
+  MOE_TRACE_CTA(trace, 2);
   for (int t = blockIdx.x; t < T; t += gridDim.x) {
     const int kt = __ldg(tok_nloc + t);
     if (kt == 1) continue;
@@ -47,11 +50,13 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const int* tok
       *reinterpret_cast<uint2*>(out + static_cast<size_t>(t) * kH + 4 * v) = pk;
     }
   }
+  (void)trace;
+  MOE_TRACE_CTA(trace, 1);
 }
 
 // Launched as a programmatic dependent of GEMM2.
 cudaError_t combine_launch(int T, int grid, cudaStream_t st, const int* tok_nloc, const int* tok_rows,
-                           const float* part2, uint16_t* out) {
+                           const float* part2, uint16_t* out, unsigned long long* trace) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kCombineThreads);
@@ -61,7 +66,7 @@ cudaError_t combine_launch(int T, int grid, cudaStream_t st, const int* tok_nloc
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, combine_kernel, tok_nloc, tok_rows, part2, out, T);
+  return cudaLaunchKernelEx(&cfg, combine_kernel, tok_nloc, tok_rows, part2, out, T, trace);
 }
 
 }  // namespace moe

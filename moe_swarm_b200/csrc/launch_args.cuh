@@ -39,8 +39,21 @@ struct RouteArgs {
   float* row_weight;
   uint8_t* a_perm;
   float* sa_perm;
+  unsigned long long* trace;   // [2][kMaxSms][kTraceSlots]: routing, scatter (MOE_TRACE builds)
 };
 
+
+// Start / end time of a CTA in a traced build (MOE_TRACE): slots [0] and [1] of the CTA's
+// record, CTAs beyond kMaxSms unrecorded.
+#ifdef MOE_TRACE
+#define MOE_TRACE_CTA(base, slot)                                                          \
+  do {                                                                                     \
+    if ((base) && threadIdx.x == 0 && blockIdx.x < kMaxSms)                                \
+      (base)[blockIdx.x * kTraceSlots + (slot)] = globaltimer_ns();                        \
+  } while (0)
+#else
+#define MOE_TRACE_CTA(base, slot) (void)0
+#endif
 
 // Records `msg` as this thread's last error (moe_b200_last_error) and returns `code`.
 int report_error(int code, const char* msg);

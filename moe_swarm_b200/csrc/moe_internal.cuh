@@ -26,7 +26,8 @@ constexpr int kTok = 32;          // token tile (MMA N) of the streaming kernels
 constexpr int kMaxSms = 256;      // partial-slot capacity of the stream-K fixup (2 per CTA)
 constexpr int kStreamMaxT = 512;  // T above which the wide (token-major) kernels run
 constexpr int kTraceSlots = 16;   // per-CTA counters of a traced build (MOE_TRACE)
-constexpr int kTraceKernels = 4;  // stream GEMM1, stream GEMM2, wide GEMM1, wide GEMM2
+constexpr int kTraceKernels = 8;  // stream GEMM1, stream GEMM2, wide GEMM1, wide GEMM2, routing,
+                                  // scatter, GEMM1 finalize, combine
 
 // Device status codes (first one wins).
 enum : int {

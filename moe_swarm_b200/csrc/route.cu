@@ -14,9 +14,12 @@
 // own group g), 8 tokens per CTA.  Local picks are counted per 128-token chunk with global
 // atomics (order-independent sums).  The last CTA to finish (a self-resetting arrival
 // counter) turns the chunk counts into expert segment starts, per-chunk bases and the GEMM
-// tile tables (plan) and zeroes the counts for the next call.  scatter_kernel: 8 tokens per
-// CTA; the rank of a token in an expert's segment is a popcount over the chunk's per-expert
-// token bitmask plus the chunk base.
+// tile tables (plan) and zeroes the counts for the next call.  scatter_kernel (a programmatic
+// dependent of route_kernel): 8 tokens per CTA; the rank of a token in an expert's segment is
+// a popcount over the chunk's per-expert token bitmask plus the chunk base.  At decode sizes
+// one CTA does all of it in one launch with the pick lists and counts in shared memory.  Each
+// routing CTA first starts its tokens' hidden rows and scales toward L2, so the permutation's
+// copies find them there.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -80,10 +83,42 @@ __device__ __forceinline__ float exp_to_f32(double y) {
   return static_cast<float>(p * scale);
 }
 
+// Where routing leaves each token's local picks for the permutation: global memory when the
+// permutation is a separate launch (scatter_kernel), shared memory when one CTA does both.
+struct PickBuf {
+  int* le;     // [T][8] local expert ids, ascending
+  float* lw;   // [T][8] their combine weights
+  int* nloc;   // [T] local pick counts (also written to RouteArgs::tok_nloc for the combine)
+  int* hist;   // [nchunks][E] per-chunk counts of local picks
+};
+
+__device__ __forceinline__ PickBuf global_picks(const RouteArgs& a) {
+  return PickBuf{a.tok_le, a.tok_lw, a.tok_nloc, a.chunk_hist};
+}
+
+// Starts tokens [t0, t0 + nt) on their way to L2: their logits rows and, when the activation
+// rows are copied, their hidden rows and 56 scales -- so those loads find L2 rather than HBM
+// once the routing, which needs none of them but the logits, is done.
+__device__ void prefetch_tokens(const RouteArgs& a, int t0, int nt, int tid, int nthr) {
+  if (nt <= 0) return;
+  if (a.logits) {
+    const char* lg = reinterpret_cast<const char*>(a.logits + static_cast<size_t>(t0) * kEG);
+    for (int i = tid; i < nt * (kEG * 4 / 128); i += nthr) prefetch_l2(lg + static_cast<size_t>(i) * 128);
+  }
+  if (!a.a_perm || !a.hidden) return;
+  const uint8_t* h = a.hidden + static_cast<size_t>(t0) * kH;
+  for (int i = tid; i < nt * (kH / 128); i += nthr) prefetch_l2(h + static_cast<size_t>(i) * 128);
+  // scales [56][T]: the run of nt floats of each K-block, its first and last line
+  for (int i = tid; i < 2 * kKB1; i += nthr) {
+    const int kb = i >> 1;
+    prefetch_l2(a.hs_scale + static_cast<size_t>(kb) * a.T + t0 + ((i & 1) ? nt - 1 : 0));
+  }
+}
+
 // Routes token t with the calling warp: writes its top-8 (ascending expert id) with weights,
 // its local picks (ascending local expert) and their count, and adds the local picks to the
 // token's chunk histogram.
-__device__ void route_token(const RouteArgs& a, const float* s_bias, int t, int lane) {
+__device__ void route_token(const RouteArgs& a, const PickBuf& pb, const float* s_bias, int t, int lane) {
   const float* lg = a.logits + static_cast<size_t>(t) * kEG + lane * 8;
   const float4 v0 = *reinterpret_cast<const float4*>(lg);
   const float4 v1 = *reinterpret_cast<const float4*>(lg + 4);
@@ -175,9 +210,9 @@ __device__ void route_token(const RouteArgs& a, const float* s_bias, int t, int 
   int lpos = warp_excl_prefix(__popc(local_mask), lane);
   int* idx_out = a.topk_idx + static_cast<size_t>(t) * kTopK;
   float* w_out = a.topk_w + static_cast<size_t>(t) * kTopK;
-  int* le_out = a.tok_le + static_cast<size_t>(t) * kTopK;
-  float* lw_out = a.tok_lw + static_cast<size_t>(t) * kTopK;
-  int* hist = a.chunk_hist + static_cast<size_t>(t / kChunk) * a.E;
+  int* le_out = pb.le + static_cast<size_t>(t) * kTopK;
+  float* lw_out = pb.lw + static_cast<size_t>(t) * kTopK;
+  int* hist = pb.hist + static_cast<size_t>(t / kChunk) * a.E;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     if ((taken >> i) & 1u) {
@@ -198,14 +233,17 @@ __device__ void route_token(const RouteArgs& a, const float* s_bias, int t, int 
   int nloc = __popc(local_mask);
 #pragma unroll
   for (int d = 16; d >= 1; d >>= 1) nloc += __shfl_xor_sync(0xffffffffu, nloc, d);
-  if (lane == 0) a.tok_nloc[t] = nloc;
+  if (lane == 0) {
+    a.tok_nloc[t] = nloc;
+    pb.nloc[t] = nloc;
+  }
 }
 
 // Pre-routed token t (moe_b200_forward_routed): the caller's 8 picks (global expert id and
 // combine weight) take the place of the routing.  Lanes 0..7 hold the picks; the local ones are
 // written in ascending expert order -- the row order of the permutation and the order of the
 // combine's sum -- and counted in the token's chunk histogram.  A token's ids must be distinct.
-__device__ void pick_token(const RouteArgs& a, int t, int lane) {
+__device__ void pick_token(const RouteArgs& a, const PickBuf& pb, int t, int lane) {
   int ge = -1;
   float w = 0.f;
   if (lane < kTopK) {
@@ -224,16 +262,19 @@ __device__ void pick_token(const RouteArgs& a, int t, int lane) {
   }
   if (local) {
     const int le = ge - a.offset;
-    a.tok_le[static_cast<size_t>(t) * kTopK + rank] = le;
-    a.tok_lw[static_cast<size_t>(t) * kTopK + rank] = w;
-    atomicAdd(a.chunk_hist + static_cast<size_t>(t / kChunk) * a.E + le, 1);
+    pb.le[static_cast<size_t>(t) * kTopK + rank] = le;
+    pb.lw[static_cast<size_t>(t) * kTopK + rank] = w;
+    atomicAdd(pb.hist + static_cast<size_t>(t / kChunk) * a.E + le, 1);
   }
   const int nloc = __popc(__ballot_sync(0xffffffffu, local));
-  if (lane == 0) a.tok_nloc[t] = nloc;
+  if (lane == 0) {
+    a.tok_nloc[t] = nloc;
+    pb.nloc[t] = nloc;
+  }
 }
 
 // Per-expert token bitmask of chunk c, built by the whole CTA from the tokens' pick lists.
-__device__ void build_chunk_masks(const RouteArgs& a, int c, uint32_t (*s_mask)[kChunk / 32]) {
+__device__ void build_chunk_masks(const RouteArgs& a, const PickBuf& pb, int c, uint32_t (*s_mask)[kChunk / 32]) {
   for (int i = threadIdx.x; i < a.E * (kChunk / 32); i += blockDim.x) (&s_mask[0][0])[i] = 0;
   __syncthreads();
   const int t0 = c * kChunk;
@@ -241,8 +282,8 @@ __device__ void build_chunk_masks(const RouteArgs& a, int c, uint32_t (*s_mask)[
   for (int i = threadIdx.x; i < nt * kTopK; i += blockDim.x) {
     const int tl = i / kTopK, p = i % kTopK;
     const int t = t0 + tl;
-    if (p < __ldcg(a.tok_nloc + t)) {
-      const int le = __ldcg(a.tok_le + static_cast<size_t>(t) * kTopK + p);
+    if (p < pb.nloc[t]) {
+      const int le = pb.le[static_cast<size_t>(t) * kTopK + p];
       atomicOr(&s_mask[le][tl >> 5], 1u << (tl & 31));
     }
   }
@@ -252,9 +293,9 @@ __device__ void build_chunk_masks(const RouteArgs& a, int c, uint32_t (*s_mask)[
 // Scatters the local picks of token t (index tl in its chunk) with the calling warp: row
 // indices, row metadata, the fp8 activation row and its 56 scales.  A token with no local
 // expert gets a zero output row instead.
-__device__ void scatter_token(const RouteArgs& a, int t, int tl, int lane,
+__device__ void scatter_token(const RouteArgs& a, const PickBuf& pb, int t, int tl, int lane,
                               const uint32_t (*s_mask)[kChunk / 32], const int* base) {
-  const int k = __ldcg(a.tok_nloc + t);
+  const int k = pb.nloc[t];
   if (k == 0) {
     if (a.out == nullptr) return;
     uint4* dst = reinterpret_cast<uint4*>(a.out + static_cast<size_t>(t) * kH);
@@ -263,8 +304,8 @@ __device__ void scatter_token(const RouteArgs& a, int t, int tl, int lane,
   }
   int row = 0;
   if (lane < k) {
-    const int le = __ldcg(a.tok_le + static_cast<size_t>(t) * kTopK + lane);
-    const float w = __ldcg(a.tok_lw + static_cast<size_t>(t) * kTopK + lane);
+    const int le = pb.le[static_cast<size_t>(t) * kTopK + lane];
+    const float w = pb.lw[static_cast<size_t>(t) * kTopK + lane];
     int rank = 0;
     for (int wd = 0; wd < (tl >> 5); ++wd) rank += __popc(s_mask[le][wd]);
     rank += __popc(s_mask[le][tl >> 5] & ((1u << (tl & 31)) - 1u));
@@ -305,76 +346,94 @@ __device__ void scatter_token(const RouteArgs& a, int t, int tl, int lane,
 }
 
 // Chunk counts -> expert segment starts, per-chunk bases, tile prefixes and the plan.
-// Run by one whole CTA (blockDim >= 256); zeroes the chunk counts for the next call.
-__device__ void scan_plan(const RouteArgs& a, int* s_tmp, int* s_start) {
+// Run by one whole CTA (blockDim >= 256).  `hist` / `cbase` are [nchunks][E]: in global memory
+// (GLOBAL, filled by atomics of other CTAs; the counts are zeroed here for the next call) or
+// in this CTA's shared memory.
+template <bool GLOBAL>
+__device__ void scan_plan(const RouteArgs& a, int* hist, int* cbase, int* s_tmp) {
   const int tid = threadIdx.x;
   const int E = a.E;
+  auto rd = [&](size_t i) { return GLOBAL ? __ldcg(hist + i) : hist[i]; };
   int cnt = 0;
+  int first[8] = {};   // the first eight chunks' counts, kept for the base pass below
   if (tid < E)
     for (int c0 = 0; c0 < a.nchunks; c0 += 8) {
       int v[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j)
-        v[j] = c0 + j < a.nchunks ? __ldcg(a.chunk_hist + static_cast<size_t>(c0 + j) * E + tid) : 0;
+        v[j] = c0 + j < a.nchunks ? rd(static_cast<size_t>(c0 + j) * E + tid) : 0;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) cnt += v[j];
+      for (int j = 0; j < 8; ++j) {
+        cnt += v[j];
+        if (c0 == 0) first[j] = v[j];
+      }
     }
-  // inclusive scans over experts of rows and of 128- and 32-row tiles
-  int* s_cnt = s_tmp;
-  int* s_mt = s_tmp + 256;
-  int* s_tt = s_tmp + 512;
+  // inclusive scans over experts (threads 0..255) of rows and of 128- and 32-row tiles: a
+  // shuffle scan inside each warp, then each thread adds the totals of the warps before it
+  const int lane = tid & 31, warp = tid >> 5;
+  const int ucnt = tid < E ? cnt : 0;
+  const int umt = (ucnt + kBlk - 1) / kBlk, utt = (ucnt + kTok - 1) / kTok;
+  int x0 = ucnt, x1 = umt, x2 = utt;
   if (tid < 256) {
-    const bool on = tid < E;
-    s_cnt[tid] = on ? cnt : 0;
-    s_mt[tid] = on ? (cnt + kBlk - 1) / kBlk : 0;
-    s_tt[tid] = on ? (cnt + kTok - 1) / kTok : 0;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int y0 = __shfl_up_sync(0xffffffffu, x0, d);
+      const int y1 = __shfl_up_sync(0xffffffffu, x1, d);
+      const int y2 = __shfl_up_sync(0xffffffffu, x2, d);
+      if (lane >= d) {
+        x0 += y0;
+        x1 += y1;
+        x2 += y2;
+      }
+    }
+    if (lane == 31) {
+      s_tmp[warp] = x0;
+      s_tmp[8 + warp] = x1;
+      s_tmp[16 + warp] = x2;
+    }
   }
   __syncthreads();
-  for (int d = 1; d < 256; d <<= 1) {
-    int v0 = 0, v1 = 0, v3 = 0;
-    if (tid < 256 && tid >= d) {
-      v0 = s_cnt[tid - d];
-      v1 = s_mt[tid - d];
-      v3 = s_tt[tid - d];
+  int rows = 0, mtiles = 0, ttiles = 0;
+  if (tid < 256) {
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      const int w0 = s_tmp[w], w1 = s_tmp[8 + w], w2 = s_tmp[16 + w];
+      if (w < warp) {
+        x0 += w0;
+        x1 += w1;
+        x2 += w2;
+      }
+      rows += w0;
+      mtiles += w1;
+      ttiles += w2;
     }
-    __syncthreads();
-    if (tid < 256 && tid >= d) {
-      s_cnt[tid] += v0;
-      s_mt[tid] += v1;
-      s_tt[tid] += v3;
-    }
-    __syncthreads();
   }
-  const int rows = s_cnt[255];
-  const int mtiles = s_mt[255];
   if (tid == 0) {
     Plan p{};
     p.T = a.T;
     p.E = E;
     p.rows = rows;
     p.m_tiles = mtiles;
-    p.tt = s_tt[255];
+    p.tt = ttiles;
     *a.plan = p;
   }
   if (tid < E) {
-    const int start = s_cnt[tid] - cnt;
-    const int mt0 = s_mt[tid] - (cnt + kBlk - 1) / kBlk;
-    s_start[tid] = start;
+    const int start = x0 - cnt;
     a.e_count[tid] = cnt;
     a.e_start[tid] = start;
-    a.e_mt_start[tid] = mt0;
-    a.e_tt[tid] = s_tt[tid] - (cnt + kTok - 1) / kTok;
+    a.e_mt_start[tid] = x1 - umt;
+    a.e_tt[tid] = x2 - utt;
     int run = start;
     for (int c0 = 0; c0 < a.nchunks; c0 += 8) {
       int v[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j)
-        v[j] = c0 + j < a.nchunks ? __ldcg(a.chunk_hist + static_cast<size_t>(c0 + j) * E + tid) : 0;
+        v[j] = c0 == 0 ? first[j] : c0 + j < a.nchunks ? rd(static_cast<size_t>(c0 + j) * E + tid) : 0;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         if (c0 + j < a.nchunks) {
-          a.chunk_base[static_cast<size_t>(c0 + j) * E + tid] = run;
-          a.chunk_hist[static_cast<size_t>(c0 + j) * E + tid] = 0;   // self-reset for the next call
+          cbase[static_cast<size_t>(c0 + j) * E + tid] = run;
+          if (GLOBAL) hist[static_cast<size_t>(c0 + j) * E + tid] = 0;   // self-reset for the next call
         }
         run += v[j];
       }
@@ -383,24 +442,28 @@ __device__ void scan_plan(const RouteArgs& a, int* s_tmp, int* s_start) {
   if (tid == 0) {
     a.e_start[E] = rows;
     a.e_mt_start[E] = mtiles;
-    a.e_tt[E] = s_tt[255];
+    a.e_tt[E] = ttiles;
   }
   __syncthreads();
 }
 
 __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
   __shared__ float s_bias[kEG];
-  __shared__ int s_tmp[1024];
-  __shared__ int s_start[kEG];
+  __shared__ int s_tmp[32];   // per-warp totals of the expert scans
   __shared__ int s_last;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  MOE_TRACE_CTA(a.trace, 0);
+  pdl_launch_dependents();   // scatter_kernel's CTAs may become resident meanwhile
+  const int tb = blockIdx.x * kRouteWarps;
+  prefetch_tokens(a, tb, min(kRouteWarps, a.T - tb), tid, blockDim.x);
   if (!a.pre_idx)   // pre-routed calls have no logits or bias
     for (int i = tid; i < kEG; i += blockDim.x) s_bias[i] = bf16_bits_to_float(a.bias[i]);
   __syncthreads();
-  const int t = blockIdx.x * kRouteWarps + warp;
+  const PickBuf pb = global_picks(a);
+  const int t = tb + warp;
   if (t < a.T) {
-    if (a.pre_idx) pick_token(a, t, lane);
-    else route_token(a, s_bias, t, lane);
+    if (a.pre_idx) pick_token(a, pb, t, lane);
+    else route_token(a, pb, s_bias, t, lane);
   }
   __threadfence();
   __syncthreads();
@@ -409,23 +472,31 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(RouteArgs a) {
     s_last = (prev == static_cast<int>(gridDim.x) - 1);
   }
   __syncthreads();
+  MOE_TRACE_CTA(a.trace, 1);
   if (!s_last) return;
   __threadfence();
-  scan_plan(a, s_tmp, s_start);
+  scan_plan<true>(a, a.chunk_hist, a.chunk_base, s_tmp);
   if (tid == 0) *a.route_done = 0;   // self-reset for the next call
+  MOE_TRACE_CTA(a.trace, 1);
 }
 
 __global__ void __launch_bounds__(kRouteThreads) scatter_kernel(RouteArgs a) {
   __shared__ uint32_t s_mask[kEG][kChunk / 32];
   __shared__ int s_base[kEG];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  pdl_launch_dependents();
+  unsigned long long* tr = a.trace ? a.trace + kMaxSms * kTraceSlots : nullptr;
+  MOE_TRACE_CTA(tr, 0);
+  pdl_wait();                // the picks and the chunk bases come from route_kernel
+  pdl_launch_dependents();   // GEMM1 may run its prologue meanwhile
+  const PickBuf pb = global_picks(a);
   const int t0 = blockIdx.x * kRouteWarps;   // this CTA's tokens: t0 .. t0+7 (one chunk)
   const int c = t0 / kChunk;
   for (int e = threadIdx.x; e < a.E; e += blockDim.x) s_base[e] = a.chunk_base[static_cast<size_t>(c) * a.E + e];
-  build_chunk_masks(a, c, s_mask);
+  build_chunk_masks(a, pb, c, s_mask);
   const int t = t0 + warp;
-  if (t < a.T) scatter_token(a, t, t - c * kChunk, lane, s_mask, s_base);
+  if (t < a.T) scatter_token(a, pb, t, t - c * kChunk, lane, s_mask, s_base);
+  (void)tr;
+  MOE_TRACE_CTA(tr, 1);
 }
 
 // T <= kRouteSmallT: one CTA routes every token (one warp each, a single round), scans and
@@ -435,35 +506,53 @@ __global__ void __launch_bounds__(kRouteThreads) scatter_kernel(RouteArgs a) {
 // permute with scatter_kernel on as many CTAs.
 constexpr int kRouteSmallT = 32;
 constexpr int kRouteSmallThreads = 1024;
-
+// The one-CTA body for T <= MAXT (route_small_kernel: kRouteSmallT; the no-alloc entry point:
+// kNoAllocMaxT).  Its pick lists, chunk counts and chunk bases live in shared memory, so the
+// scan and the permutation read them without an L2 round trip; sized by MAXT so that the
+// decode kernel leaves room on its SM for a GEMM CTA.
+template <int MAXT>
 __device__ __forceinline__ void route_small_body(const RouteArgs& a) {
+  constexpr int kChunks = (MAXT + kChunk - 1) / kChunk;
   __shared__ float s_bias[kEG];
   __shared__ uint32_t s_mask[kEG][kChunk / 32];
-  __shared__ int s_tmp[1024];
-  __shared__ int s_start[kEG];
+  __shared__ int s_tmp[32];   // per-warp totals of the expert scans
   __shared__ int s_base[kEG];
+  __shared__ int s_le[MAXT * kTopK];
+  __shared__ float s_lw[MAXT * kTopK];
+  __shared__ int s_nloc[MAXT];
+  __shared__ int s_hist[kChunks * kEG];
+  __shared__ int s_cbase[kChunks * kEG];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  prefetch_tokens(a, 0, a.T, tid, blockDim.x);
   if (!a.pre_idx)   // pre-routed calls have no logits or bias
     for (int i = tid; i < kEG; i += blockDim.x) s_bias[i] = bf16_bits_to_float(a.bias[i]);
+  for (int i = tid; i < a.nchunks * a.E; i += blockDim.x) s_hist[i] = 0;
   __syncthreads();
+  MOE_TRACE_CTA(a.trace, 2);
+  const PickBuf pb{s_le, s_lw, s_nloc, s_hist};
   for (int t = warp; t < a.T; t += kRouteSmallThreads / 32) {
-    if (a.pre_idx) pick_token(a, t, lane);
-    else route_token(a, s_bias, t, lane);
+    if (a.pre_idx) pick_token(a, pb, t, lane);
+    else route_token(a, pb, s_bias, t, lane);
   }
   __syncthreads();
-  scan_plan(a, s_tmp, s_start);
+  MOE_TRACE_CTA(a.trace, 3);
+  scan_plan<false>(a, s_hist, s_cbase, s_tmp);
+  MOE_TRACE_CTA(a.trace, 4);
   for (int c = 0; c < a.nchunks; ++c) {
-    for (int e = tid; e < a.E; e += blockDim.x) s_base[e] = c == 0 ? s_start[e] : __ldcg(a.chunk_base + static_cast<size_t>(c) * a.E + e);
-    build_chunk_masks(a, c, s_mask);
+    for (int e = tid; e < a.E; e += blockDim.x) s_base[e] = s_cbase[c * a.E + e];
+    build_chunk_masks(a, pb, c, s_mask);
+    MOE_TRACE_CTA(a.trace, 5);
     const int t0 = c * kChunk, nt = min(kChunk, a.T - t0);
-    for (int tl = warp; tl < nt; tl += kRouteSmallThreads / 32) scatter_token(a, t0 + tl, tl, lane, s_mask, s_base);
+    for (int tl = warp; tl < nt; tl += kRouteSmallThreads / 32) scatter_token(a, pb, t0 + tl, tl, lane, s_mask, s_base);
     __syncthreads();
   }
 }
 
 __global__ void __launch_bounds__(kRouteSmallThreads, 1) route_small_kernel(RouteArgs a) {
+  MOE_TRACE_CTA(a.trace, 0);
   pdl_launch_dependents();   // the GEMM that follows may run its prologue meanwhile
-  route_small_body(a);
+  route_small_body<kRouteSmallT>(a);
+  MOE_TRACE_CTA(a.trace, 1);
 }
 
 cudaError_t route_launch(const RouteArgs& a, cudaStream_t st, int* launches) {
@@ -475,9 +564,21 @@ cudaError_t route_launch(const RouteArgs& a, cudaStream_t st, int* launches) {
   const int grid = (a.T + kRouteWarps - 1) / kRouteWarps;
   route_kernel<<<grid, kRouteThreads, 0, st>>>(a);
   ++*launches;
-  scatter_kernel<<<grid, kRouteThreads, 0, st>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  // a programmatic dependent of route_kernel: its CTAs wait resident for the routing
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kRouteThreads);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, scatter_kernel, a);
   ++*launches;
-  return cudaGetLastError();
+  return e;
 }
 
 // ---------------------------------------------------------------------------------------
@@ -493,7 +594,7 @@ constexpr size_t kNoAllocScratchBytes = 64 * 1024;
 static __device__ __align__(256) unsigned char g_route_scratch[kNoAllocScratchBytes];
 
 struct NoAllocLayout {
-  size_t plan, chunk_hist, chunk_base, tok_le, tok_lw, tok_nloc, tok_rows, tables, total;
+  size_t plan, tok_nloc, tok_rows, tables, total;
 };
 
 __host__ __device__ constexpr size_t na_align(size_t x) { return (x + 255) / 256 * 256; }
@@ -501,11 +602,7 @@ __host__ __device__ constexpr size_t na_align(size_t x) { return (x + 255) / 256
 __host__ __device__ constexpr NoAllocLayout noalloc_layout() {
   NoAllocLayout l{};
   l.plan = 0;
-  l.chunk_hist = na_align(l.plan + sizeof(Plan));
-  l.chunk_base = na_align(l.chunk_hist + 2 * kEG * sizeof(int));
-  l.tok_le = na_align(l.chunk_base + 2 * kEG * sizeof(int));
-  l.tok_lw = na_align(l.tok_le + kNoAllocMaxT * kTopK * sizeof(int));
-  l.tok_nloc = na_align(l.tok_lw + kNoAllocMaxT * kTopK * sizeof(float));
+  l.tok_nloc = na_align(l.plan + sizeof(Plan));
   l.tok_rows = na_align(l.tok_nloc + kNoAllocMaxT * sizeof(int));
   l.tables = na_align(l.tok_rows + kNoAllocMaxT * kTopK * sizeof(int));
   l.total = na_align(l.tables + 3 * (kEG + 1) * sizeof(int));
@@ -514,10 +611,7 @@ __host__ __device__ constexpr NoAllocLayout noalloc_layout() {
 static_assert(noalloc_layout().total <= kNoAllocScratchBytes, "no-alloc scratch too small");
 
 __global__ void __launch_bounds__(kRouteSmallThreads, 1) route_noalloc_kernel(RouteArgs a) {
-  // the chunk counts must start at zero; the array keeps the previous call's contents
-  for (int i = threadIdx.x; i < 2 * kEG; i += blockDim.x) a.chunk_hist[i] = 0;
-  __syncthreads();
-  route_small_body(a);
+  route_small_body<kNoAllocMaxT>(a);   // counts in shared memory: nothing carries over between calls
 }
 
 }  // namespace moe
@@ -581,11 +675,7 @@ extern "C" MOE_B200_API int moe_b200_route_noalloc(const moe_b200_args* args, in
   r.topk_idx = topk_idx;
   r.topk_w = topk_w;
   r.tok_nloc = reinterpret_cast<int*>(sp + L.tok_nloc);
-  r.tok_le = reinterpret_cast<int*>(sp + L.tok_le);
-  r.tok_lw = reinterpret_cast<float*>(sp + L.tok_lw);
-  r.tok_rows = reinterpret_cast<int*>(sp + L.tok_rows);
-  r.chunk_hist = reinterpret_cast<int*>(sp + L.chunk_hist);
-  r.chunk_base = reinterpret_cast<int*>(sp + L.chunk_base);
+  r.tok_rows = reinterpret_cast<int*>(sp + L.tok_rows);   // pick lists and counts: shared memory
   int* tab = reinterpret_cast<int*>(sp + L.tables);
   r.e_count = expert_count;
   r.e_start = tab;

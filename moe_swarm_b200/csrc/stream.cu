@@ -41,7 +41,8 @@ namespace moe {
 // waiting for a free stage, [3] K-blocks issued, [4] MMA cycles waiting for data, [5] MMA
 // cycles waiting for a free TMEM buffer, [6] epilogue cycles waiting for an accumulator,
 // [7] epilogue promotion cycles, [8] tile-epilogue cycles, [9] stream-K fixup cycles,
-// [10] scale-staging cycles, [11] first data arrival ns.
+// [10] scale-staging cycles, [11] first data arrival ns, [12] MMA issue cycles (after the
+// waits, through the commits), [13] MMA thread end ns.
 #ifdef MOE_TRACE
 #define MOE_TCLK() clock64()
 #define MOE_TADD(var, t0) (var) += clock64() - (t0)
@@ -216,7 +217,7 @@ __device__ void s_mma(StreamSmem<MODE>& sm, uint32_t tmem, const TileArgs& g, co
   constexpr int ST = SCfg<MODE>::STAGES;
   constexpr uint32_t idesc = idesc_e4m3_f32(128, kTok);
   uint32_t stage = 0, phase = 0, tk = 0, buf = 0;
-  long long tw_t = 0, tw_f = 0, t_first = 0;
+  long long tw_t = 0, tw_f = 0, t_first = 0, t_iss = 0;
   SegIter it(sk, blockIdx.x);
   int tile, k0, k1;
   while (it.next(tile, k0, k1)) {
@@ -232,6 +233,7 @@ __device__ void s_mma(StreamSmem<MODE>& sm, uint32_t tmem, const TileArgs& g, co
       if (t_first == 0) t_first = static_cast<long long>(globaltimer_ns());
 #endif
       tc_fence_after();
+      t0 = MOE_TCLK();
       {
         const uint32_t st = smem_u32(sm.stage[stage]);
         const uint32_t d = tmem + buf * 64u;
@@ -250,6 +252,7 @@ __device__ void s_mma(StreamSmem<MODE>& sm, uint32_t tmem, const TileArgs& g, co
       }
       mma_commit(&sm.empty[stage]);
       mma_commit(&sm.tfull[buf]);
+      MOE_TADD(t_iss, t0);
       tk ^= 1u << buf;
       buf = (buf + 1) & (kSBufs - 1);
       if (++stage == ST) {
@@ -266,6 +269,8 @@ done:
   g.trace[blockIdx.x * kTraceSlots + 4] = tw_f;
   g.trace[blockIdx.x * kTraceSlots + 5] = tw_t;
   g.trace[blockIdx.x * kTraceSlots + 11] = t_first;
+  g.trace[blockIdx.x * kTraceSlots + 12] = t_iss;
+  g.trace[blockIdx.x * kTraceSlots + 13] = globaltimer_ns();
 #endif
 }
 
@@ -574,65 +579,98 @@ cudaError_t stream_prepare() {
                               static_cast<int>(stream_smem_bytes<2>()));
 }
 
-// Launched as programmatic dependents of the preceding kernel in the stream (PDL).
-// Shared memory of stream_fin1_kernel: the tile tables and the MODE 1 epilogue's buffers.
+// Shared memory of stream_fin1_kernel: the tile tables.
 struct FinSmem {
-  uint8_t ostage[2][kTok][128];
-  float colmax[4][kTok];
-  float amax[kTok];
   int e_cnt[kEG + 1];
   int e_start[kEG + 1];
   int e_tt[kEG + 1];
 };
+constexpr int kFinThreads = 256;
 
-// GEMM1 tiles that stream-K split over several CTAs: the contributors' partial accumulators
-// summed in CTA order (deterministic; the same sums in the same order as a last-arriver fixup)
-// followed by the tile epilogue (SwiGLU, hi/lo e4m3).  One CTA of 128 threads per split tile,
-// thread = weight row; G is the GEMM's grid, which fixes its tile split.
-__global__ void __launch_bounds__(kSEpiThreads) stream_fin1_kernel(TileArgs g, int G) {
+// GEMM1 tiles that stream-K split over several CTAs, finished one (tile, token column) pair per
+// warp: the contributors' partial accumulators summed in CTA order (deterministic; the same sums
+// in the same order as a last-arriver fixup), then the column's SwiGLU, its amax over the tile's
+// 128 features (a warp reduction) and its hi/lo e4m3 bytes -- element for element the arithmetic
+// of s_epi1.  Lane l owns features 4l..4l+3: one float4 of X1 and one of X2 per contributor, and
+// one 4-byte store each of the column's hi and lo bytes, so a column is one round of loads and
+// two coalesced 128-byte stores with no block barrier.  Pairs are numbered column-major
+// (p = column * nsplit + split tile), so at decode sizes, where a tile holds one or two tokens,
+// the live pairs fall on distinct warps.  G is the GEMM's grid, which fixes its tile split.
+__global__ void __launch_bounds__(kFinThreads) stream_fin1_kernel(TileArgs g, int G) {
   __shared__ FinSmem sm;
+  MOE_TRACE_CTA(g.trace, 0);
   pdl_wait();                 // the partials come from GEMM1
+  MOE_TRACE_CTA(g.trace, 2);
   pdl_launch_dependents();    // GEMM2 may start its prologue and weight prefetch
   const Plan plan = *g.plan;
-  Sched sk;
-  sk.init(plan.tt * SCfg<1>::NT, G, SCfg<1>::KB);
-  const int nsplit = sk.tiles - sk.dp;   // stream-K tiles
-  if (static_cast<int>(blockIdx.x) >= nsplit) return;
+  // the tables do not depend on the plan: their loads go out together with the plan's
   for (int i = threadIdx.x; i <= g.E; i += blockDim.x) {
     sm.e_cnt[i] = i < g.E ? g.e_count[i] : 0;
     sm.e_start[i] = g.e_start[i];
     sm.e_tt[i] = g.e_tiles[i];
   }
+  Sched sk;
+  sk.init(plan.tt * SCfg<1>::NT, G, SCfg<1>::KB);
+  const int nsplit = sk.tiles - sk.dp;   // stream-K tiles
   __syncthreads();
-  const int q = threadIdx.x >> 5, lane = threadIdx.x & 31, r = threadIdx.x;
-  for (int i = blockIdx.x; i < nsplit; i += gridDim.x) {
-    const int tile = sk.dp + i;
+  const int lane = threadIdx.x & 31;
+  constexpr int kWarps = kFinThreads / 32;
+  const int nwarps = static_cast<int>(gridDim.x) * kWarps;
+  for (int p = static_cast<int>(blockIdx.x) * kWarps + (threadIdx.x >> 5); p < nsplit * kTok; p += nwarps) {
+    const int c = p / nsplit;
+    const int tile = sk.dp + (p - c * nsplit);
     const int c0 = sk.first_cta(tile), c1 = sk.last_cta(tile);
     if (c0 == c1) continue;   // one contributor: the GEMM finished this tile itself
     const STile s = s_decode<1>(sm, g.E, tile);
-    float acc1[kTok], acc2[kTok];
+    if (c >= s.nr) continue;  // no token in this column
+    float4 x1 = make_float4(0.f, 0.f, 0.f, 0.f), x2 = x1;
+    for (int cta = c0; cta <= c1; cta += 4) {
+      float4 v1[4], v2[4];
 #pragma unroll
-    for (int c = 0; c < kTok; ++c) {
-      acc1[c] = 0.f;
-      acc2[c] = 0.f;
-    }
-    for (int cta = c0; cta <= c1; ++cta) {
-      const float* pp = g.part + static_cast<size_t>(sk.slot(cta, tile)) * 2 * kTok * 128;
+      for (int j = 0; j < 4; ++j) {
+        if (cta + j > c1) break;
+        const float* pp = g.part + static_cast<size_t>(sk.slot(cta + j, tile)) * 2 * kTok * 128 + c * 128 + 4 * lane;
+        v1[j] = __ldcg(reinterpret_cast<const float4*>(pp));
+        v2[j] = __ldcg(reinterpret_cast<const float4*>(pp + kTok * 128));
+      }
 #pragma unroll
-      for (int c = 0; c < kTok; ++c) {
-        acc1[c] += __ldcg(pp + c * 128 + r);
-        acc2[c] += __ldcg(pp + (kTok + c) * 128 + r);
+      for (int j = 0; j < 4; ++j) {
+        if (cta + j > c1) break;
+        x1.x += v1[j].x;
+        x1.y += v1[j].y;
+        x1.z += v1[j].z;
+        x1.w += v1[j].w;
+        x2.x += v2[j].x;
+        x2.y += v2[j].y;
+        x2.z += v2[j].z;
+        x2.w += v2[j].w;
       }
     }
-    s_epi1(sm, g, s, acc1, acc2, q, lane);
+    const float v0 = silu_f(x2.x) * x1.x, v1 = silu_f(x2.y) * x1.y;
+    const float v2 = silu_f(x2.z) * x1.z, v3 = silu_f(x2.w) * x1.w;
+    float m = fmaxf(fmaxf(fabsf(v0), fabsf(v1)), fmaxf(fabsf(v2), fabsf(v3)));
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    if (lane == 0) g.c_scale[static_cast<size_t>(s.nt) * g.r_pad + s.row0 + c] = m > 0.f ? m / 448.0f : 1.0f;
+    const float inv = m > 0.f ? 448.0f / m : 0.f;
+    const float y0 = v0 * inv, y1 = v1 * inv, y2 = v2 * inv, y3 = v3 * inv;
+    const uint32_t h01 = cvt_e4m3x2(y0, y1) & 0xFFFFu, h23 = cvt_e4m3x2(y2, y3) & 0xFFFFu;
+    const float2 b01 = e4m3x2_to_f2(static_cast<uint16_t>(h01));
+    const float2 b23 = e4m3x2_to_f2(static_cast<uint16_t>(h23));
+    const uint32_t l01 = cvt_e4m3x2(y0 - b01.x, y1 - b01.y) & 0xFFFFu;
+    const uint32_t l23 = cvt_e4m3x2(y2 - b23.x, y3 - b23.y) & 0xFFFFu;
+    const size_t off = static_cast<size_t>(s.row0 + c) * kI + s.nt * kBlk + 4 * lane;
+    *reinterpret_cast<uint32_t*>(g.c_hi + off) = h01 | (h23 << 16);
+    *reinterpret_cast<uint32_t*>(g.c_lo + off) = l01 | (l23 << 16);
   }
+  MOE_TRACE_CTA(g.trace, 1);
 }
 
 // Launched as a programmatic dependent of GEMM1.
 cudaError_t stream_fin_launch(int G, cudaStream_t st, const TileArgs& g) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(G);
-  cfg.blockDim = dim3(kSEpiThreads);
+  cfg.blockDim = dim3(kFinThreads);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
