@@ -139,6 +139,7 @@ moe::RouteArgs make_route_args(const moe_b200_args* a, uint8_t* ws, const moe::L
   r.e_tt = reinterpret_cast<int*>(ws + L.e_tt);
   r.row_token = reinterpret_cast<int*>(ws + L.row_token);
   r.row_weight = reinterpret_cast<float*>(ws + L.row_weight);
+  r.row_nloc = reinterpret_cast<int*>(ws + L.row_nloc);
   r.a_perm = ws + L.a_perm;
   r.sa_perm = reinterpret_cast<float*>(ws + L.sa_perm);
   r.trace = reinterpret_cast<unsigned long long*>(ws + L.trace) + 4 * (size_t)moe::kMaxSms * moe::kTraceSlots;
@@ -274,6 +275,7 @@ moe::TileArgs tile_args(const moe_b200_args* a, uint8_t* ws, const moe::Layout& 
   s.tile_cnt = reinterpret_cast<int*>(ws + L.sk_cnt);
   s.row_token = reinterpret_cast<const int*>(ws + L.row_token);
   s.row_weight = reinterpret_cast<const float*>(ws + L.row_weight);
+  s.row_nloc = reinterpret_cast<const int*>(ws + L.row_nloc);
   s.tok_nloc = reinterpret_cast<const int*>(ws + L.tok_nloc);
   s.tok_rows = reinterpret_cast<const int*>(ws + L.tok_rows);
   s.part2 = reinterpret_cast<float*>(ws + L.part2);

@@ -37,6 +37,7 @@ struct RouteArgs {
   int* e_tt;
   int* row_token;
   float* row_weight;
+  int* row_nloc;     // per row: its token's local expert count (null: not recorded)
   uint8_t* a_perm;
   float* sa_perm;
   unsigned long long* trace;   // [2][kMaxSms][kTraceSlots]: routing, scatter (MOE_TRACE builds)
@@ -75,6 +76,7 @@ struct TileArgs {
   int* tile_cnt;     // stream-K per-tile arrival counters (self-resetting)
   const int* row_token;
   const float* row_weight;
+  const int* row_nloc;
   const int* tok_nloc;
   const int* tok_rows;
   float* part2;

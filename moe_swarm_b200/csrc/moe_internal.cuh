@@ -56,7 +56,7 @@ struct Layout {
   size_t chunk_hist, chunk_base;
   size_t e_count, e_start, e_mt_start, e_tt;
   size_t sk_part, sk_cnt, trace;
-  size_t row_token, row_weight;
+  size_t row_token, row_weight, row_nloc;
   size_t a_perm, sa_perm;
   size_t c_hi, c_lo, c_scale;
   size_t part2;
@@ -104,6 +104,7 @@ inline bool compute_layout(int T, int E, Layout* L) {
   l.e_tt = take((size_t)(E + 1) * sizeof(int));
   l.row_token = take(l.r_pad * sizeof(int));
   l.row_weight = take(l.r_pad * sizeof(float));
+  l.row_nloc = take(l.r_pad * sizeof(int));   // the row's token's local expert count
   l.a_perm = take(l.r_pad * kH);
   l.sa_perm = take((size_t)kKB1 * l.r_pad * sizeof(float));
   l.c_hi = take(l.r_pad * kI);

@@ -312,6 +312,7 @@ __device__ void scatter_token(const RouteArgs& a, const PickBuf& pb, int t, int 
     row = base[le] + rank;
     a.row_token[row] = t;
     a.row_weight[row] = w;
+    if (a.row_nloc) a.row_nloc[row] = k;
     a.tok_rows[static_cast<size_t>(t) * kTopK + lane] = row;
   }
   int rows[kTopK];

@@ -14,8 +14,9 @@
 //     summed and finished by stream_fin1_kernel, a programmatic dependent of this kernel, so
 //     no CTA's range ends with a latency-bound fixup and epilogue on the critical path.
 //   MODE 2 (GEMM2): tile = (expert, 32-token tile, 128 output features nt); K = 16 blocks.
-//       D = W2 . C_hi^T + W2 . C_lo^T   (one accumulator: hi and lo share every scale)
-//       acc[r][c] += D[r][c] * s2[e, nt, kb] * sc[token c, kb]
+//       D = W2 . [C_hi; C_lo]^T   (one N = 64 MMA: columns c and 32 + c are token c's hi and
+//                                  lo products, which share every scale)
+//       acc[r][c] += (D[r][c] + D[r][32 + c]) * s2[e, nt, kb] * sc[token c, kb]
 //     epilogue: out[t, f] = bf16(w * O) for a token with one local expert; otherwise w * O
 //     goes to the token's fp32 partial row, summed in ascending expert order by the combine
 //     kernel (combine.cu) -- deterministic.  A split tile is finished by its last contributor.
@@ -86,9 +87,9 @@ struct StreamSmem {
   uint32_t tmem_base;
   int abort;
   int flag;
-  int col_t[kTok];
-  int col_k[kTok];
-  float col_w[kTok];
+  int col_t[2][kTok];     // MODE 2 tile metadata, by segment parity: token,
+  int col_k[2][kTok];     // its local expert count
+  float col_w[2][kTok];   // and the row's combine weight
   float colmax[4][kTok];
   float amax[kTok];
   int e_cnt[kEG + 1];
@@ -216,6 +217,7 @@ template <int MODE>
 __device__ void s_mma(StreamSmem<MODE>& sm, uint32_t tmem, const TileArgs& g, const Sched& sk) {
   constexpr int ST = SCfg<MODE>::STAGES;
   constexpr uint32_t idesc = idesc_e4m3_f32(128, kTok);
+  constexpr uint32_t idesc_hilo = idesc_e4m3_f32(128, 2 * kTok);   // MODE 2: B = [C_hi; C_lo]
   uint32_t stage = 0, phase = 0, tk = 0, buf = 0;
   long long tw_t = 0, tw_f = 0, t_first = 0, t_iss = 0;
   SegIter it(sk, blockIdx.x);
@@ -244,9 +246,10 @@ __device__ void s_mma(StreamSmem<MODE>& sm, uint32_t tmem, const TileArgs& g, co
             mma_f8f6f4(d, sdesc_k128_sw128(st + 32 * k), bt, idesc, k > 0);
             mma_f8f6f4(d + 32u, sdesc_k128_sw128(st + 16384 + 32 * k), bt, idesc, k > 0);
           } else {
-            const uint64_t aw = sdesc_k128_sw128(st + 32 * k);
-            mma_f8f6f4(d, aw, sdesc_k128_sw128(st + 16384 + 32 * k), idesc, k > 0);
-            mma_f8f6f4(d, aw, sdesc_k128_sw128(st + 16384 + kTok * 128 + 32 * k), idesc, 1);
+            // the hi and lo token tiles lie back to back in the stage (same 128-byte swizzle,
+            // 1024-byte aligned), so together they are one 64-row B operand: one N = 64 MMA
+            // gives W2.C_hi in columns 0..31 and W2.C_lo in 32..63, reading W2 once
+            mma_f8f6f4(d, sdesc_k128_sw128(st + 32 * k), sdesc_k128_sw128(st + 16384 + 32 * k), idesc_hilo, k > 0);
           }
         }
       }
@@ -322,29 +325,17 @@ __device__ void s_epi1(SM& sm, const TileArgs& g, const STile& s, float* x1, con
 
 // MODE 2 tile epilogue: for each token column, the bf16 output row directly when the token
 // has one local expert, otherwise the routing-weighted fp32 row for the combine kernel.
+// The metadata was staged with the segment's scales (col_*[par]).
 __device__ void s_epi2(StreamSmem<2>& sm, const TileArgs& g, const STile& s, const float* acc, int q,
-                       int lane) {
+                       int lane, int par) {
   const int r = q * 32 + lane;
   const int f = s.nt * kBlk + r;
-  if (q == 0) {   // lane c loads token column c's metadata (one round of loads for the tile)
-    int t = 0, kt = 0;
-    float w = 0.f;
-    if (lane < s.nr) {
-      t = __ldg(g.row_token + s.row0 + lane);
-      w = __ldg(g.row_weight + s.row0 + lane);
-      kt = __ldg(g.tok_nloc + t);
-    }
-    sm.col_t[lane] = t;
-    sm.col_k[lane] = kt;
-    sm.col_w[lane] = w;
-  }
-  named_bar_sync(1, kSEpiThreads);
 #pragma unroll
   for (int c = 0; c < kTok; ++c) {
     if (c >= s.nr) break;
-    const float v = __fmul_rn(acc[c], sm.col_w[c]);
-    if (sm.col_k[c] == 1)
-      g.out[static_cast<size_t>(sm.col_t[c]) * kH + f] = bf16_bits(v);
+    const float v = __fmul_rn(acc[c], sm.col_w[par][c]);
+    if (sm.col_k[par][c] == 1)
+      g.out[static_cast<size_t>(sm.col_t[par][c]) * kH + f] = bf16_bits(v);
     else
       g.part2[static_cast<size_t>(s.row0 + c) * kH + f] = v;
   }
@@ -362,7 +353,9 @@ __device__ void s_epilogue(StreamSmem<MODE>& sm, uint32_t tmem, const TileArgs& 
   if (MODE == 2) pdl_wait();   // the C scales and the combine inputs come from GEMM1
   SegIter it(sk, blockIdx.x);
   int tile, k0, k1;
+  int par = 1;   // segment parity (the double-buffered tile metadata)
   while (it.next(tile, k0, k1)) {
+    par ^= 1;
     const STile s = s_decode<MODE>(sm, g.E, tile);
     long long t0 = MOE_TCLK();
     // lane c prefetches the scale of token column c (clamped to a routed row of this tile)
@@ -390,6 +383,14 @@ __device__ void s_epilogue(StreamSmem<MODE>& sm, uint32_t tmem, const TileArgs& 
         sm.ssw[0][i] = __ldg(swp1 + k0 + i);
         sm.ssw[1][i] = __ldg(swp2 + k0 + i);
       }
+    // MODE 2: the tile epilogue's metadata, in the same round of loads (lane c: token column c).
+    // Double-buffered by segment parity: warps may still read the previous segment's copy.
+    if (MODE == 2 && q == 1) {
+      const bool live = lane < s.nr;
+      sm.col_t[par][lane] = live ? __ldg(g.row_token + s.row0 + lane) : 0;
+      sm.col_w[par][lane] = live ? __ldg(g.row_weight + s.row0 + lane) : 0.f;
+      sm.col_k[par][lane] = live ? __ldg(g.row_nloc + s.row0 + lane) : 0;
+    }
     named_bar_sync(1, kSEpiThreads);
     MOE_TADD(ts, t0);
     for (int kb = k0; kb < k1; ++kb) {
@@ -403,10 +404,7 @@ __device__ void s_epilogue(StreamSmem<MODE>& sm, uint32_t tmem, const TileArgs& 
       if (!dead) {
         tc_fence_after();
         float d1[kTok], d2[kTok];
-        if (MODE == 1)
-          tmem_ld32x2_wait(lane_base + buf * 64u, lane_base + buf * 64u + 32u, d1, d2);
-        else
-          tmem_ld16x2_wait(lane_base + buf * 64u, lane_base + buf * 64u + 16u, d1, d1 + 16);
+        tmem_ld32x2_wait(lane_base + buf * 64u, lane_base + buf * 64u + 32u, d1, d2);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.tempty[buf]);
@@ -419,7 +417,7 @@ __device__ void s_epilogue(StreamSmem<MODE>& sm, uint32_t tmem, const TileArgs& 
             acc1[c] = fmaf(d1[c], sc * w1, acc1[c]);
             acc2[c] = fmaf(d2[c], sc * w2, acc2[c]);
           } else {
-            acc1[c] = fmaf(d1[c], sc * w1, acc1[c]);
+            acc1[c] = fmaf(d1[c] + d2[c], sc * w1, acc1[c]);   // hi and lo share every scale
           }
         }
       }
@@ -487,7 +485,7 @@ __device__ void s_epilogue(StreamSmem<MODE>& sm, uint32_t tmem, const TileArgs& 
     if (MODE == 1)
       s_epi1(reinterpret_cast<StreamSmem<1>&>(sm), g, s, acc1, acc2, q, lane);
     else
-      s_epi2(reinterpret_cast<StreamSmem<2>&>(sm), g, s, acc1, q, lane);
+      s_epi2(reinterpret_cast<StreamSmem<2>&>(sm), g, s, acc1, q, lane, par);
     MOE_TADD(te, t0);
   }
 #ifdef MOE_TRACE
