@@ -250,7 +250,8 @@ namespace {
 int launch_combine(const moe_b200_args* a, uint8_t* ws, const moe::Layout& L, int sms, cudaStream_t st,
                    int* launches) {
   const int T = a->num_tokens;
-  const int grid = T < 8 * sms ? T : 8 * sms;
+  const long items = static_cast<long>(moe::kCombineChunks) * T;   // (token, row chunk) pairs
+  const int grid = items < 8L * sms ? static_cast<int>(items) : 8 * sms;
   cudaError_t e = moe::combine_launch(T, grid, st, reinterpret_cast<const int*>(ws + L.tok_nloc),
                                       reinterpret_cast<const int*>(ws + L.tok_rows),
                                       reinterpret_cast<const float*>(ws + L.part2), a->output,

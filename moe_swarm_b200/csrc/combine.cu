@@ -12,7 +12,11 @@
 
 namespace moe {
 
-constexpr int kCombineThreads = 256;
+static_assert(kCombineChunks * kCombineThreads * 4 == kH, "a row is a whole number of chunks");
+
+// Work item i = (token i / 7, chunk i % 7): each thread owns one float4 of the chunk, so a
+// token's partial rows are read in one round of independent loads, and at decode sizes the
+// row's chunks spread over seven SMs.
 
 __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const int* tok_nloc, const int* tok_rows,
                                                                   const float* part2, uint16_t* out, int T,
@@ -20,18 +24,19 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const int* tok
   MOE_TRACE_CTA(trace, 0);
   pdl_wait();   // the partial rows come from GEMM2
   MOE_TRACE_CTA(trace, 2);
-  for (int t = blockIdx.x; t < T; t += gridDim.x) {
+  for (int i = blockIdx.x; i < T * kCombineChunks; i += gridDim.x) {
+    const int t = i / kCombineChunks;
+    const int v = (i - t * kCombineChunks) * kCombineThreads + threadIdx.x;   // float4 index in the row
     const int kt = __ldg(tok_nloc + t);
     if (kt == 1) continue;
-    if (kt == 0) {
-      uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(t) * kH);
-      for (int v = threadIdx.x; v < kH * 2 / 16; v += kCombineThreads) dst[v] = make_uint4(0, 0, 0, 0);
+    if (kt == 0) {   // no local expert: this thread's 4 bf16 of the zero row
+      reinterpret_cast<uint2*>(out + static_cast<size_t>(t) * kH)[v] = make_uint2(0, 0);
       continue;
     }
     int rows[kTopK];
 #pragma unroll
     for (int a = 0; a < kTopK; ++a) rows[a] = a < kt ? __ldg(tok_rows + static_cast<size_t>(t) * kTopK + a) : 0;
-    for (int v = threadIdx.x; v < kH / 4; v += kCombineThreads) {
+    {
       float4 x[kTopK];
 #pragma unroll
       for (int a = 0; a < kTopK; ++a)

@@ -22,6 +22,8 @@ constexpr int kNT2 = kH / kBlk;   // 56 GEMM2 tiles (128 output features each)
 constexpr int kChunk = 128;       // tokens per rank-mask chunk of the permutation
 constexpr int kRouteWarps = 8;    // routing / scatter CTAs: one token per warp
 constexpr int kRouteThreads = kRouteWarps * 32;
+constexpr int kCombineThreads = 256;                      // combine CTA: one float4 per thread
+constexpr int kCombineChunks = kH / 4 / kCombineThreads;  // 7 row chunks per token
 constexpr int kTok = 32;          // token tile (MMA N) of the streaming kernels
 constexpr int kMaxSms = 256;      // partial-slot capacity of the stream-K fixup (2 per CTA)
 constexpr int kStreamMaxT = 512;  // T above which the wide (token-major) kernels run

@@ -427,28 +427,23 @@ __device__ void s_epilogue(StreamSmem<MODE>& sm, uint32_t tmem, const TileArgs& 
     }
     t0 = MOE_TCLK();
     const bool full = (k0 == 0 && k1 == SCfg<MODE>::KB);
-    if (MODE == 1 && !full) {
-      // GEMM1: leave the partial for stream_fin1_kernel, which sums the contributors of every
-      // split tile after this kernel, so no CTA ends its range waiting on the slowest one
-      const int slot = sk.slot(blockIdx.x, tile);
-      float* p = g.part + static_cast<size_t>(slot) * 2 * kTok * 128;
-#pragma unroll
-      for (int c = 0; c < kTok; ++c) {
-        p[c * 128 + r] = acc1[c];
-        p[(kTok + c) * 128 + r] = acc2[c];
-      }
-      MOE_TADD(tf, t0);
-      continue;
-    }
     if (!full) {
-      // stream-K fixup: publish this CTA's partial, the last contributor sums them in CTA order
+      // A split tile's partial, its live token columns only (the readers skip the rest).
+      // GEMM1 leaves it for stream_fin1_kernel, which sums the contributors of every split tile
+      // after this kernel, so no CTA ends its range waiting on the slowest one; GEMM2's last
+      // contributor sums them here, in CTA order.
       constexpr int NH = MODE == 1 ? 2 : 1;
       const int slot = sk.slot(blockIdx.x, tile);
       float* p = g.part + static_cast<size_t>(slot) * NH * kTok * 128;
 #pragma unroll
       for (int c = 0; c < kTok; ++c) {
+        if (c >= s.nr) break;
         p[c * 128 + r] = acc1[c];
         if (MODE == 1) p[(kTok + c) * 128 + r] = acc2[c];
+      }
+      if (MODE == 1) {
+        MOE_TADD(tf, t0);
+        continue;
       }
       named_bar_sync(1, kSEpiThreads);
       if (q == 0 && lane == 0) {
@@ -466,16 +461,27 @@ __device__ void s_epilogue(StreamSmem<MODE>& sm, uint32_t tmem, const TileArgs& 
         continue;
       }
 #pragma unroll
-      for (int c = 0; c < kTok; ++c) {
-        acc1[c] = 0.f;
-        acc2[c] = 0.f;
-      }
-      for (int cta = sk.first_cta(tile); cta <= sk.last_cta(tile); ++cta) {
-        const float* pp = g.part + static_cast<size_t>(sk.slot(cta, tile)) * NH * kTok * 128;
+      for (int c = 0; c < kTok; ++c) acc1[c] = 0.f;
+      // live columns in blocks of 8; the loads of up to four contributors go out together
+      const int c0 = sk.first_cta(tile), c1 = sk.last_cta(tile);
 #pragma unroll
-        for (int c = 0; c < kTok; ++c) {
-          acc1[c] += __ldcg(pp + c * 128 + r);
-          if (MODE == 1) acc2[c] += __ldcg(pp + (kTok + c) * 128 + r);
+      for (int cb = 0; cb < kTok; cb += 8) {
+        if (cb >= s.nr) break;
+        for (int cta = c0; cta <= c1; cta += 4) {
+          float v[4][8];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            if (cta + j > c1) break;
+            const float* pp = g.part + static_cast<size_t>(sk.slot(cta + j, tile)) * NH * kTok * 128 + cb * 128 + r;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) v[j][c] = __ldcg(pp + c * 128);
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            if (cta + j > c1) break;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) acc1[cb + c] += v[j][c];
+          }
         }
       }
     }
