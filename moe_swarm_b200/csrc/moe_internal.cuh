@@ -39,6 +39,7 @@ enum : int {
   kStWaitMmaTmem = 0x103,
   kStWaitEpilogue = 0x104,
   kStWaitDrain = 0x105,
+  kStWaitFixup = 0x106,   // a split tile's finisher waiting for the other contributors
 };
 
 // Written by the routing scan, read by the GEMM kernels.

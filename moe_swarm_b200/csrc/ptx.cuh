@@ -237,6 +237,38 @@ __device__ __forceinline__ int atomic_add_acq_rel_gpu(int* p, int v) {
   return old;
 }
 
+// Release-add on a global counter whose result nobody waits for: after a CTA barrier, one
+// thread publishes every store the CTA made before the barrier and signals one arrival.
+__device__ __forceinline__ void red_add_release_gpu(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Bounded wait until the counter *p reaches `target` (acquire: the arrivals' published stores
+// are visible afterwards, to the whole CTA after a barrier).  On timeout, or when another role
+// already gave up (*abort != 0), records `code` in *err and returns false.
+__device__ __forceinline__ bool counter_wait_geq(const int* p, int target, volatile int* abort, int* err,
+                                                 int code) {
+  if (ld_acquire_gpu(p) >= target) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (ld_acquire_gpu(p) >= target) return true;
+    if ((i & 63u) == 0) {
+      if (*abort) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        *abort = 1;
+        atomicCAS(err, 0, code);
+        return false;
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------- programmatic dependent launch
 // Wait until the preceding kernel in the stream has completed and its writes are visible
 // (a no-op when the kernel was not launched as a programmatic dependent).

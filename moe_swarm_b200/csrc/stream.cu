@@ -19,7 +19,8 @@
 //       acc[r][c] += (D[r][c] + D[r][32 + c]) * s2[e, nt, kb] * sc[token c, kb]
 //     epilogue: out[t, f] = bf16(w * O) for a token with one local expert; otherwise w * O
 //     goes to the token's fp32 partial row, summed in ascending expert order by the combine
-//     kernel (combine.cu) -- deterministic.  A split tile is finished by its last contributor.
+//     kernel (combine.cu) -- deterministic.  A split tile is finished by its first contributor,
+//     which in stream-K order reaches it last and adds the others' partials in CTA order.
 //
 // Work is split stream-K over the persistent CTAs (sched.cuh), so all SMs stream weights
 // even when routing activates a few experts.  CTA = 6 warps: warp 0 TMA producer, warp 1
@@ -86,7 +87,6 @@ struct StreamSmem {
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
-  int flag;
   int col_t[2][kTok];     // MODE 2 tile metadata, by segment parity: token,
   int col_k[2][kTok];     // its local expert count
   float col_w[2][kTok];   // and the row's combine weight
@@ -428,46 +428,41 @@ __device__ void s_epilogue(StreamSmem<MODE>& sm, uint32_t tmem, const TileArgs& 
     t0 = MOE_TCLK();
     const bool full = (k0 == 0 && k1 == SCfg<MODE>::KB);
     if (!full) {
-      // A split tile's partial, its live token columns only (the readers skip the rest).
-      // GEMM1 leaves it for stream_fin1_kernel, which sums the contributors of every split tile
-      // after this kernel, so no CTA ends its range waiting on the slowest one; GEMM2's last
-      // contributor sums them here, in CTA order.
+      // A split tile.  In stream-K order its first contributor (k0 == 0) reaches its segment at
+      // the end of its range, the others earlier, so the first contributor finishes the tile:
+      // the others store their partial (live token columns only) and signal one arrival without
+      // waiting for anything; the finisher waits for those arrivals (normally all in already)
+      // and adds their partials to its own in CTA order.  GEMM1's split tiles are all finished
+      // by stream_fin1_kernel after this kernel instead, so there every contributor stores.
       constexpr int NH = MODE == 1 ? 2 : 1;
-      const int slot = sk.slot(blockIdx.x, tile);
-      float* p = g.part + static_cast<size_t>(slot) * NH * kTok * 128;
+      const bool finisher = MODE == 2 && k0 == 0;
+      if (!finisher) {
+        const int slot = sk.slot(blockIdx.x, tile);
+        float* p = g.part + static_cast<size_t>(slot) * NH * kTok * 128;
 #pragma unroll
-      for (int c = 0; c < kTok; ++c) {
-        if (c >= s.nr) break;
-        p[c * 128 + r] = acc1[c];
-        if (MODE == 1) p[(kTok + c) * 128 + r] = acc2[c];
-      }
-      if (MODE == 1) {
+        for (int c = 0; c < kTok; ++c) {
+          if (c >= s.nr) break;
+          p[c * 128 + r] = acc1[c];
+          if (MODE == 1) p[(kTok + c) * 128 + r] = acc2[c];
+        }
+        if (MODE == 2) {
+          named_bar_sync(1, kSEpiThreads);   // the four warps' stores, then one release
+          if (q == 0 && lane == 0) red_add_release_gpu(g.tile_cnt + tile, 1);
+        }
         MOE_TADD(tf, t0);
         continue;
       }
-      named_bar_sync(1, kSEpiThreads);
+      const int c0 = static_cast<int>(blockIdx.x), c1 = sk.last_cta(tile);
       if (q == 0 && lane == 0) {
-        const int expect = sk.last_cta(tile) - sk.first_cta(tile) + 1;
-        const int prev = atomic_add_acq_rel_gpu(g.tile_cnt + tile, 1);
-        const int last = prev == expect - 1;
-        if (last) g.tile_cnt[tile] = 0;
-        sm.flag = last;
+        if (counter_wait_geq(g.tile_cnt + tile, c1 - c0, &sm.abort, g.status, kStWaitFixup))
+          g.tile_cnt[tile] = 0;   // every other contributor has arrived: reset for the next call
       }
       named_bar_sync(1, kSEpiThreads);
-      const int last = sm.flag;
-      named_bar_sync(1, kSEpiThreads);
-      if (!last) {
-        MOE_TADD(tf, t0);
-        continue;
-      }
-#pragma unroll
-      for (int c = 0; c < kTok; ++c) acc1[c] = 0.f;
       // live columns in blocks of 8; the loads of up to four contributors go out together
-      const int c0 = sk.first_cta(tile), c1 = sk.last_cta(tile);
 #pragma unroll
       for (int cb = 0; cb < kTok; cb += 8) {
         if (cb >= s.nr) break;
-        for (int cta = c0; cta <= c1; cta += 4) {
+        for (int cta = c0 + 1; cta <= c1; cta += 4) {
           float v[4][8];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
