@@ -168,6 +168,41 @@ __device__ __forceinline__ void tmem_ld16x2_wait(uint32_t ta, uint32_t tb, float
   }
 }
 
+// Issue only: two loads of 32 lanes x 16 consecutive 32-bit columns, at TMEM addresses ta
+// (into r[0..15]) and tb (into r[16..31]).  The registers hold the data only after
+// tmem_wait_ld32(r); a load issued after that wait overlaps whatever runs before the next one.
+__device__ __forceinline__ void tmem_ld16x2_issue(uint32_t ta, uint32_t tb, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(ta));
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+        "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),
+        "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(tb));
+}
+
+// tcgen05.wait::ld naming the 32 destination registers of the outstanding tmem_ld16x2_issue,
+// so that no use of them is scheduled above the wait.
+__device__ __forceinline__ void tmem_wait_ld32(uint32_t* r) {
+  asm volatile(
+      "tcgen05.wait::ld.sync.aligned;"
+      : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),
+        "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]),
+        "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]),
+        "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]),
+        "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]),
+        "+r"(r[31])
+      :
+      : "memory");
+}
+
 // Two loads of 32 lanes x 32 consecutive 32-bit columns, then tcgen05.wait::ld (the wait
 // names every destination register so no use of a loaded value is scheduled above it).
 __device__ __forceinline__ void tmem_ld32x2_wait(uint32_t ta, uint32_t tb, float* a, float* b) {

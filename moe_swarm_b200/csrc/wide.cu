@@ -405,8 +405,15 @@ __device__ __forceinline__ void w_epilogue(WideSmem<MODE>& sm, uint32_t tmem, co
     for (int j = 0; j < (MODE == 1 ? 64 : 128); ++j) acc1[j] = 0.f;
 #pragma unroll
     for (int j = 0; j < (MODE == 1 ? 64 : 1); ++j) acc2[j] = 0.f;
+    // this segment's weight scales, each read one K-block ahead of its use
+    float wa_n = sm.ssw[MODE == 1 ? 0 : h][0], wb_n = sm.ssw[MODE == 1 ? 1 : h][0];
     for (int kb = k0; kb < k1; ++kb) {
       const int ki = kb - k0;
+      const float wa = wa_n, wb = wb_n;
+      if (ki + 1 < k1 - k0) {
+        wa_n = sm.ssw[MODE == 1 ? 0 : h][ki + 1];
+        wb_n = sm.ssw[MODE == 1 ? 1 : h][ki + 1];
+      }
       const float sa = pf0;
       pf0 = pf1;
       pf1 = pf2;
@@ -423,56 +430,55 @@ __device__ __forceinline__ void w_epilogue(WideSmem<MODE>& sm, uint32_t tmem, co
         if (lane == 0) mbar_arrive(&sm.tempty[buf]);
       }
       if (!dead && qlive) {
+        // Promotion in four steps of 2 x 16 columns (MODE 1: X1 and X2 columns 64h + 16s ..;
+        // MODE 2: columns 128h + 32s ..).  Each step's TMEM load is issued before the previous
+        // step's FMAs, so its latency hides behind them; the buffer goes back to the MMA as
+        // soon as the last load has landed.
         tc_fence_after();
         const uint32_t base = lane_base + buf * 256u;
-        if (MODE == 1) {
-          const float f1 = sa * sm.ssw[0][ki], f2 = sa * sm.ssw[1][ki];
-          const float2 f1v = make_float2(f1, f1), f2v = make_float2(f2, f2);
+        const float fa = sa * wa, fb = sa * wb;
+        const float2 fav = make_float2(fa, fa), fbv = make_float2(fb, fb);
+        auto col_a = [&](int st) -> uint32_t {
+          return MODE == 1 ? base + 64u * h + 16u * st : base + 128u * h + 32u * st;
+        };
+        auto col_b = [&](int st) -> uint32_t {
+          return MODE == 1 ? base + 128u + 64u * h + 16u * st : base + 128u * h + 32u * st + 16u;
+        };
+        uint32_t ra[32], rb[32];
+        tmem_ld16x2_issue(col_a(0), col_b(0), ra);
+        tmem_wait_ld32(ra);
 #pragma unroll
-          for (int c0 = 0; c0 < 64; c0 += 32) {
-            float d1[32], d2[32];
-            tmem_ld32x2_wait(base + 64u * h + c0, base + 128u + 64u * h + c0, d1, d2);
-            if (c0 == 32) {
-              tc_fence_before();
-              __syncwarp();
-              if (lane == 0) mbar_arrive(&sm.tempty[buf]);
-            }
-#pragma unroll
-            for (int j = 0; j < 32; j += 2) {
-              float2 a1 = make_float2(acc1[c0 + j], acc1[c0 + j + 1]);
-              float2 a2 = make_float2(acc2[c0 + j], acc2[c0 + j + 1]);
-              a1 = __ffma2_rn(make_float2(d1[j], d1[j + 1]), f1v, a1);
-              a2 = __ffma2_rn(make_float2(d2[j], d2[j + 1]), f2v, a2);
-              acc1[c0 + j] = a1.x;
-              acc1[c0 + j + 1] = a1.y;
-              acc2[c0 + j] = a2.x;
-              acc2[c0 + j + 1] = a2.y;
-            }
+        for (int st = 0; st < 4; ++st) {
+          uint32_t* cur = (st & 1) ? rb : ra;
+          uint32_t* nxt = (st & 1) ? ra : rb;
+          if (st < 3) {
+            tmem_ld16x2_issue(col_a(st + 1), col_b(st + 1), nxt);
+          } else {   // every TMEM read of this buffer has completed
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.tempty[buf]);
           }
-        } else {
-          const float f = sa * sm.ssw[h][ki];
-          const float2 fv = make_float2(f, f);
-#pragma unroll
-          for (int c0 = 0; c0 < 128; c0 += 64) {
-            float d1[32], d2[32];
-            tmem_ld32x2_wait(base + 128u * h + c0, base + 128u * h + c0 + 32u, d1, d2);
-            if (c0 == 64) {
-              tc_fence_before();
-              __syncwarp();
-              if (lane == 0) mbar_arrive(&sm.tempty[buf]);
-            }
-#pragma unroll
-            for (int j = 0; j < 32; j += 2) {
-              float2 a1 = make_float2(acc1[c0 + j], acc1[c0 + j + 1]);
-              float2 a2 = make_float2(acc1[c0 + 32 + j], acc1[c0 + 32 + j + 1]);
-              a1 = __ffma2_rn(make_float2(d1[j], d1[j + 1]), fv, a1);
-              a2 = __ffma2_rn(make_float2(d2[j], d2[j + 1]), fv, a2);
-              acc1[c0 + j] = a1.x;
-              acc1[c0 + j + 1] = a1.y;
-              acc1[c0 + 32 + j] = a2.x;
-              acc1[c0 + 32 + j + 1] = a2.y;
-            }
+          float* acc_a;
+          float* acc_b;
+          if constexpr (MODE == 1) {
+            acc_a = acc1 + 16 * st;
+            acc_b = acc2 + 16 * st;
+          } else {
+            acc_a = acc1 + 32 * st;
+            acc_b = acc1 + 32 * st + 16;
           }
+#pragma unroll
+          for (int j = 0; j < 16; j += 2) {
+            float2 a1 = make_float2(acc_a[j], acc_a[j + 1]);
+            float2 a2 = make_float2(acc_b[j], acc_b[j + 1]);
+            a1 = __ffma2_rn(make_float2(__uint_as_float(cur[j]), __uint_as_float(cur[j + 1])), fav, a1);
+            a2 = __ffma2_rn(make_float2(__uint_as_float(cur[16 + j]), __uint_as_float(cur[17 + j])), fbv, a2);
+            acc_a[j] = a1.x;
+            acc_a[j + 1] = a1.y;
+            acc_b[j] = a2.x;
+            acc_b[j + 1] = a2.y;
+          }
+          if (st < 3) tmem_wait_ld32(nxt);
         }
       }
       MOE_WADD(tp, t0);
