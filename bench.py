@@ -60,8 +60,8 @@ def peaks():
 
 
 # ----------------------------------------------------------------------------- clocks
-class ClockSampler:
-    """nvidia-smi clock/throttle samples during the timed region (read-only queries)."""
+class _SmiSampler:
+    """nvidia-smi clock/throttle samples (read-only queries): the fallback when NVML is absent."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -115,7 +115,77 @@ class ClockSampler:
         sm.sort()
         loaded = [s for s in sm if s > 0.5 * mx] or sm
         return {"sm_mhz": loaded[len(loaded) // 2], "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": "nvidia-smi"}
+
+
+class ClockSampler:
+    """SM clock and clock-event reasons of this process's GPU during the timed region.
+
+    A thread reads them through NVML every 10 ms (read-only queries) from start() to stop();
+    the report keeps the samples taken between the host timestamps mark_begin() / mark_end()
+    placed around the timed steps (the GPU runs them in that interval), so even a timed region
+    of a few tens of milliseconds carries several samples.  Falls back to nvidia-smi when NVML
+    is not available."""
+    REASONS = ((0x4, "sw_power_cap"), (0x8, "hw_slowdown"), (0x20, "sw_thermal_slowdown"),
+               (0x40, "hw_thermal_slowdown"), (0x80, "hw_power_brake_slowdown"))
+
+    def __init__(self, device):
+        self.samples = []
+        self.t0 = self.t1 = None
+        self.halt = threading.Event()
+        self.thread = None
+        self.smi = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            p = torch.cuda.get_device_properties(device)
+            bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+            self.nv = pynvml
+            self.handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM))
+            self.reasons_of = (getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None)
+                               or pynvml.nvmlDeviceGetCurrentClocksThrottleReasons)
+        except Exception:
+            self.handle = None
+            self.smi = _SmiSampler()
+
+    def _run(self):
+        while not self.halt.is_set():
+            try:
+                mhz = float(self.nv.nvmlDeviceGetClockInfo(self.handle, self.nv.NVML_CLOCK_SM))
+                bits = int(self.reasons_of(self.handle))
+                self.samples.append((time.perf_counter(), mhz, bits))
+            except Exception:
+                pass
+            self.halt.wait(0.01)
+
+    def start(self):
+        if self.smi is not None:
+            self.smi.start()
+            return
+        self.thread = threading.Thread(target=self._run, daemon=True)
+        self.thread.start()
+
+    def mark_begin(self):
+        self.t0 = time.perf_counter()
+
+    def mark_end(self):
+        self.t1 = time.perf_counter()
+
+    def stop(self, gpus=None):
+        if self.smi is not None:
+            return self.smi.stop(gpus)
+        self.halt.set()
+        if self.thread is not None:
+            self.thread.join(timeout=2)
+        inside = [s for s in self.samples
+                  if self.t0 is not None and self.t1 is not None and self.t0 <= s[0] <= self.t1]
+        if not inside:
+            return None
+        sm = sorted(s[1] for s in inside)
+        reasons = sorted({name for s in inside for bit, name in self.REASONS if s[2] & bit})
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(inside), "source": "nvml, 10 ms"}
 
 
 # ----------------------------------------------------------------------------- workload
@@ -436,6 +506,9 @@ def main():
             return shard
         return out
 
+    clocks = ClockSampler(device)
+    if rank == 0:
+        clocks.start()
     for _ in range(warmup):
         step(x, False)
     torch.cuda.synchronize()
@@ -443,16 +516,15 @@ def main():
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    clocks = ClockSampler()
-    if rank == 0:
-        clocks.start()
     timer.read(reset=True)
+    clocks.mark_begin()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record()
     for _ in range(steps):
         step(x, True)
     end.record()
     torch.cuda.synchronize()
+    clocks.mark_end()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()

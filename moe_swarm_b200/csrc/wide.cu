@@ -321,20 +321,27 @@ __device__ __forceinline__ void w_store1(WideSmem<1>& sm, const TileArgs& g, con
 __device__ __forceinline__ void w_epi2(WideSmem<2>& sm, const TileArgs& g, const WTile& s, const float* acc, int ew,
                                        int h, int q, int lane, int t, float w, int kt) {
   const int rows_here = min(32, s.nr - 32 * q);
-  float* st = reinterpret_cast<float*>(sm.ostg[ew]);   // [32][20]
+  // staging [32 rows][16 floats]; the four 16-byte chunks of row r sit at chunk ^ ((r >> 1) & 3),
+  // which makes both the row-wise vector stores and the column-chunk reads bank-conflict free
+  float* st = reinterpret_cast<float*>(sm.ostg[ew]);
   sm.mt[ew][lane] = kt == 1 ? -1 - t : t;              // < 0: the bf16 output row of token -1-v
   const int col0 = s.nt * 256 + 128 * h;
+  const int swz = (lane >> 1) & 3;
   __syncwarp();
 #pragma unroll
   for (int rd = 0; rd < 8; ++rd) {
 #pragma unroll
-    for (int j = 0; j < 16; ++j) st[lane * 20 + j] = __fmul_rn(acc[16 * rd + j], w);
+    for (int c = 0; c < 4; ++c) {
+      const float* a = acc + 16 * rd + 4 * c;
+      *reinterpret_cast<float4*>(st + lane * 16 + 4 * (c ^ swz)) =
+          make_float4(__fmul_rn(a[0], w), __fmul_rn(a[1], w), __fmul_rn(a[2], w), __fmul_rn(a[3], w));
+    }
     __syncwarp();
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int r = 8 * i + (lane >> 2), ch = lane & 3;
       if (r < rows_here) {
-        const float4 v = *reinterpret_cast<const float4*>(st + r * 20 + 4 * ch);
+        const float4 v = *reinterpret_cast<const float4*>(st + r * 16 + 4 * (ch ^ ((r >> 1) & 3)));
         const int tv = sm.mt[ew][r];
         const int col = col0 + 16 * rd + 4 * ch;
         if (tv < 0) {
