@@ -436,6 +436,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-sweeps", action="store_true")
+    ap.add_argument("--ep-combine", choices=["peer", "nccl"], default="peer",
+                    help="N > 1: combine over peer memory inside the layer call (moe_b200_forward_ep), "
+                         "or the layer followed by an NCCL reduce-scatter")
     ap.add_argument("--cpu-experts", type=int, default=8)
     ap.add_argument("--workloads", default=None, metavar="FILE",
                     help="replay a flashinfer-bench workload file (jsonl): one JSON line per workload")
@@ -455,7 +458,10 @@ def main():
 
     config = {"workload": "ep_full_layer_T4096 (benchmark config 4: 256 experts sharded 256/N per GPU)",
               "T": EP_T, "experts_total": E_GLOBAL, "experts_per_gpu": E_GLOBAL // world,
-              "parallelism": f"ep{world}", "combine": "nccl reduce_scatter bf16" if world > 1 else "none",
+              "parallelism": f"ep{world}",
+              "combine": ("none" if world == 1 else
+                          "peer memory: epilogue stores into the owner's buffer over NVLink, rank-order fp32 sum "
+                          "(moe_b200_forward_ep)" if args.ep_combine == "peer" else "nccl reduce_scatter bf16"),
               "l2": "inputs larger than L2 (>=1.4 GB of routed weights per GPU per step)"}
 
     if args.impl == "reference":
@@ -498,8 +504,20 @@ def main():
     T = EP_T
     shard = torch.empty((T // world, H), dtype=torch.bfloat16, device=device)
     timer = StageTimer()
+    peer = world > 1 and args.ep_combine == "peer"
+    layer = None
+    if peer:
+        from moe_swarm_b200 import ep as EP
+        layer = EP.ExpertParallelMoE()
+
+    def layer_args(inp):
+        return (inp["routing_logits"], inp["routing_bias"], inp["hidden_states"], inp["hidden_states_scale"],
+                inp["gemm1_weights"], inp["gemm1_weights_scale"], inp["gemm2_weights"],
+                inp["gemm2_weights_scale"], inp["routed_scaling_factor"])
 
     def step(inp, use_timer):
+        if peer:   # the stage timer has no EP form: stages are timed separately below
+            return layer.forward(*layer_args(inp), combine="peer", out=shard)
         out = timer.run(inp) if use_timer else M.run(**inp)
         if world > 1:
             dist.reduce_scatter_tensor(shard, out)
@@ -529,6 +547,10 @@ def main():
         dist.barrier()
     torch.cuda.synchronize()
     ms = start.elapsed_time(end)
+    if peer:   # stage split of the same layer without the combine (untimed for the line's value)
+        for _ in range(steps):
+            timer.run(x)
+        torch.cuda.synchronize()
     stage_ms, calls = timer.read(reset=True)
     visible = None
     ck = clocks.stop(visible) if rank == 0 else None
@@ -560,7 +582,9 @@ def main():
     used = [False] * NB
 
     def layer_into(inp, dst):
-        if world > 1:
+        if peer:
+            layer.forward(*layer_args(inp), combine="peer", out=dst)
+        elif world > 1:
             dist.reduce_scatter_tensor(dst, M.run(**inp))
         else:
             M.run(**inp, out=dst)

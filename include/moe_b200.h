@@ -145,6 +145,34 @@ MOE_B200_API int moe_b200_forward_routed(const moe_b200_args* args, const int32_
                                          void* stream);
 
 /*
+ * Expert parallelism over NVLink peer memory (no counterpart in the reference, whose layer is
+ * one GPU's; it replaces the layer call followed by a separate reduce-scatter).  N ranks each
+ * hold all T tokens (T a multiple of N) and their own E_local experts (`args`, as for
+ * moe_b200_forward; args->output is not written).  Rank r owns tokens
+ * [r*shard_tokens, (r+1)*shard_tokens).  The GEMM2 and combine epilogues store every output row
+ * of this rank straight into the owning rank's receive buffer, in this rank's slot.  Each rank
+ * then waits (bounded; a timeout sets the device status) for the N slots of its tokens and
+ * sums them in rank order, in fp32 with one bf16 rounding, into out_shard.
+ *
+ * recv[r] and signal[r] are rank r's buffers, mapped in this process (e.g. torch symmetric
+ * memory): recv bf16 [2][N][shard_tokens][7168], signal uint32 [2][8], zeroed once before the
+ * first call.  `epoch` counts the calls 1, 2, 3, ..., the same on every rank; its parity
+ * selects the half of both buffers this call uses.  Every rank makes every call.
+ */
+#define MOE_B200_MAX_RANKS 8
+typedef struct moe_b200_ep {
+  int32_t world;                          /* N, 1..8 */
+  int32_t rank;                           /* this rank, 0..N-1 */
+  int32_t shard_tokens;                   /* T / N */
+  uint32_t epoch;                         /* call number, from 1 */
+  void* recv[MOE_B200_MAX_RANKS];         /* per rank: its receive buffer */
+  uint32_t* signal[MOE_B200_MAX_RANKS];   /* per rank: its flag words */
+  void* out_shard;                        /* this rank's result, bf16 [shard_tokens][7168] */
+} moe_b200_ep;
+MOE_B200_API int moe_b200_forward_ep(const moe_b200_args* args, const moe_b200_ep* ep, void* workspace,
+                                     size_t workspace_bytes, void* stream);
+
+/*
  * Routing and permutation only (the reference's _route_kernel + _pf_permute_kernel,
  * solution/python/kernel.py:137-213, :1211-1243): fills the routing arrays of the
  * layout and zeroes output rows of tokens with no local expert.

@@ -26,6 +26,7 @@ EXPORTED = (
     "moe_b200_workspace_init",
     "moe_b200_forward",
     "moe_b200_forward_routed",
+    "moe_b200_forward_ep",
     "moe_b200_route",
     "moe_b200_device_status",
     "moe_b200_last_error",
@@ -53,6 +54,22 @@ class MoeArgs(ctypes.Structure):
         ("num_local_experts", ctypes.c_int32),
         ("local_expert_offset", ctypes.c_int32),
         ("routed_scaling_factor", ctypes.c_float),
+    ]
+
+
+MAX_RANKS = 8
+
+
+class MoeEp(ctypes.Structure):
+    """moe_b200_ep: expert parallelism over peer memory (include/moe_b200.h)."""
+    _fields_ = [
+        ("world", ctypes.c_int32),
+        ("rank", ctypes.c_int32),
+        ("shard_tokens", ctypes.c_int32),
+        ("epoch", ctypes.c_uint32),
+        ("recv", ctypes.c_void_p * MAX_RANKS),
+        ("signal", ctypes.c_void_p * MAX_RANKS),
+        ("out_shard", ctypes.c_void_p),
     ]
 
 
@@ -86,6 +103,8 @@ def lib() -> ctypes.CDLL:
     l.moe_b200_forward.restype = ctypes.c_int
     l.moe_b200_forward_routed.argtypes = [ctypes.POINTER(MoeArgs), vp, vp, vp, sz, vp]
     l.moe_b200_forward_routed.restype = ctypes.c_int
+    l.moe_b200_forward_ep.argtypes = [ctypes.POINTER(MoeArgs), ctypes.POINTER(MoeEp), vp, sz, vp]
+    l.moe_b200_forward_ep.restype = ctypes.c_int
     l.moe_b200_route.argtypes = [ctypes.POINTER(MoeArgs), vp, sz, vp]
     l.moe_b200_route.restype = ctypes.c_int
     l.moe_b200_device_status.argtypes = [vp, sz, i32, i32, vp, i32]

@@ -21,7 +21,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libmoe_b200.so"
 TRACE_LIB = PKG / "libmoe_b200_trace.so"   # MOE_TRACE build: per-CTA role counters
-SOURCES = ["route.cu", "wide.cu", "stream.cu", "combine.cu", "capi.cu"]
+SOURCES = ["route.cu", "wide.cu", "stream.cu", "combine.cu", "ep.cu", "capi.cu"]
 HEADERS = ["ptx.cuh", "moe_internal.cuh", "launch_args.cuh", "sched.cuh"]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -22,10 +22,11 @@ cudaError_t wide_launch(int mode, int grid, cudaStream_t st, const CUtensorMap& 
                         const CUtensorMap& b, const TileArgs& g);
 cudaError_t stream_prepare();
 cudaError_t combine_launch(int T, int grid, cudaStream_t st, const int* tok_nloc, const int* tok_rows,
-                           const float* part2, uint16_t* out, unsigned long long* trace);
+                           const float* part2, const OutMap& out, unsigned long long* trace);
 cudaError_t stream_launch(int mode, int grid, cudaStream_t st, const CUtensorMap& w, const CUtensorMap& t,
                           const CUtensorMap& t2, const TileArgs& g);
 cudaError_t stream_fin_launch(int G, cudaStream_t st, const TileArgs& g);
+cudaError_t ep_finish_launch(const EpArgs& a, int sms, cudaStream_t st, int* launches);
 
 }  // namespace moe
 
@@ -248,13 +249,13 @@ struct moe_b200_timer {
 namespace {
 
 int launch_combine(const moe_b200_args* a, uint8_t* ws, const moe::Layout& L, int sms, cudaStream_t st,
-                   int* launches) {
+                   int* launches, const moe::OutMap& om) {
   const int T = a->num_tokens;
   const long items = static_cast<long>(moe::kCombineChunks) * T;   // (token, row chunk) pairs
   const int grid = items < 8L * sms ? static_cast<int>(items) : 8 * sms;
   cudaError_t e = moe::combine_launch(T, grid, st, reinterpret_cast<const int*>(ws + L.tok_nloc),
                                       reinterpret_cast<const int*>(ws + L.tok_rows),
-                                      reinterpret_cast<const float*>(ws + L.part2), a->output,
+                                      reinterpret_cast<const float*>(ws + L.part2), om,
                                       reinterpret_cast<unsigned long long*>(ws + L.trace) +
                                           7 * (size_t)moe::kMaxSms * moe::kTraceSlots);
   if (e != cudaSuccess) return cuda_fail(e, "combine launch");
@@ -262,7 +263,7 @@ int launch_combine(const moe_b200_args* a, uint8_t* ws, const moe::Layout& L, in
   return MOE_B200_OK;
 }
 
-moe::TileArgs tile_args(const moe_b200_args* a, uint8_t* ws, const moe::Layout& L) {
+moe::TileArgs tile_args(const moe_b200_args* a, uint8_t* ws, const moe::Layout& L, const moe::OutMap& om) {
   moe::TileArgs s{};
   s.plan = reinterpret_cast<const moe::Plan*>(ws + L.plan);
   s.e_count = reinterpret_cast<const int*>(ws + L.e_count);
@@ -280,18 +281,26 @@ moe::TileArgs tile_args(const moe_b200_args* a, uint8_t* ws, const moe::Layout& 
   s.tok_nloc = reinterpret_cast<const int*>(ws + L.tok_nloc);
   s.tok_rows = reinterpret_cast<const int*>(ws + L.tok_rows);
   s.part2 = reinterpret_cast<float*>(ws + L.part2);
-  s.out = a->output;
+  s.out = om;
   s.status = reinterpret_cast<int*>(ws + L.status);
   return s;
 }
 
+// om: where the output rows go (null: args->output).
 int forward_impl(const moe_b200_args* a, void* workspace, size_t ws_bytes, void* stream,
-                 moe_b200_timer* timer, const int32_t* pre_idx = nullptr, const float* pre_w = nullptr) {
+                 moe_b200_timer* timer, const int32_t* pre_idx = nullptr, const float* pre_w = nullptr,
+                 const moe::OutMap* om_in = nullptr) {
   g_last_launches = 0;
   moe::Layout L;
   int dev = 0;
   int rc = prepare(a, workspace, ws_bytes, &L, &dev, pre_idx != nullptr);
   if (rc) return rc;
+  moe::OutMap om{};
+  if (om_in) {
+    om = *om_in;
+  } else {
+    om.base[0] = a->output;
+  }
   if (a->num_tokens == 0) return MOE_B200_OK;
   DeviceInfo& di = device_info(dev);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -330,7 +339,7 @@ int forward_impl(const moe_b200_args* a, void* workspace, size_t ws_bytes, void*
         !encode_u8_2d(&mLo, ws + L.c_lo, moe::kI, L.r_pad, moe::kTok) ||
         !encode_u8_2d(&mW2s, a->gemm2_weights, moe::kI, (uint64_t)E * moe::kH))
       return fail(MOE_B200_ERR_CUDA, "cuTensorMapEncodeTiled failed");
-    moe::TileArgs s = tile_args(a, ws, L);
+    moe::TileArgs s = tile_args(a, ws, L, om);
     s.e_tiles = reinterpret_cast<const int*>(ws + L.e_tt);
     unsigned long long* trace = reinterpret_cast<unsigned long long*>(ws + L.trace);
     const int grid = di.sms < moe::kMaxSms ? di.sms : moe::kMaxSms;
@@ -354,7 +363,7 @@ int forward_impl(const moe_b200_args* a, void* workspace, size_t ws_bytes, void*
     e = moe::stream_launch(2, grid, st, mW2s, mHi, mLo, s2);
     if (e != cudaSuccess) return cuda_fail(e, "stream gemm2 launch");
     ++launches;
-    rc = launch_combine(a, ws, L, di.sms, st, &launches);
+    rc = launch_combine(a, ws, L, di.sms, st, &launches, om);
     if (rc) return rc;
     if (ev) cudaEventRecord(ev[3], st);
     g_last_launches = launches;
@@ -368,7 +377,7 @@ int forward_impl(const moe_b200_args* a, void* workspace, size_t ws_bytes, void*
       !encode_u8_2d(&mClo, ws + L.c_lo, moe::kI, L.r_pad, 128) ||
       !encode_u8_2d(&mW2, a->gemm2_weights, moe::kI, (uint64_t)E * moe::kH))
     return fail(MOE_B200_ERR_CUDA, "cuTensorMapEncodeTiled failed");
-  moe::TileArgs w = tile_args(a, ws, L);
+  moe::TileArgs w = tile_args(a, ws, L, om);
   unsigned long long* trace = reinterpret_cast<unsigned long long*>(ws + L.trace);
   const int grid = di.sms < moe::kMaxSms ? di.sms : moe::kMaxSms;
   moe::TileArgs w1 = w;
@@ -388,7 +397,7 @@ int forward_impl(const moe_b200_args* a, void* workspace, size_t ws_bytes, void*
   e = moe::wide_launch(2, grid, st, mChi, mClo, mW2, w2);
   if (e != cudaSuccess) return cuda_fail(e, "wide gemm2 launch");
   ++launches;
-  rc = launch_combine(a, ws, L, di.sms, st, &launches);
+  rc = launch_combine(a, ws, L, di.sms, st, &launches, om);
   if (rc) return rc;
   if (ev) cudaEventRecord(ev[3], st);
   g_last_launches = launches;
@@ -407,6 +416,53 @@ int moe_b200_forward_routed(const moe_b200_args* a, const int32_t* topk_idx, con
                             void* workspace, size_t ws_bytes, void* stream) {
   if (a && a->num_tokens > 0 && (!topk_idx || !topk_w)) return fail(MOE_B200_ERR_ARG, "null topk_idx / topk_w");
   return forward_impl(a, workspace, ws_bytes, stream, nullptr, topk_idx, topk_w);
+}
+
+int moe_b200_forward_ep(const moe_b200_args* a, const moe_b200_ep* ep, void* workspace, size_t ws_bytes,
+                        void* stream) {
+  if (!a || !ep) return fail(MOE_B200_ERR_ARG, "null args or ep");
+  const int N = ep->world, T = a->num_tokens;
+  if (N < 1 || N > MOE_B200_MAX_RANKS || ep->rank < 0 || ep->rank >= N)
+    return fail(MOE_B200_ERR_ARG, "ep: world must be in [1, 8] and rank in [0, world)");
+  if (T < 0 || ep->shard_tokens < 0 || static_cast<int64_t>(ep->shard_tokens) * N != T)
+    return fail(MOE_B200_ERR_ARG, "ep: shard_tokens * world must equal num_tokens");
+  if (ep->epoch == 0) return fail(MOE_B200_ERR_ARG, "ep: epoch counts calls from 1");
+  if (T == 0) return MOE_B200_OK;
+  if (!ep->out_shard || (reinterpret_cast<uintptr_t>(ep->out_shard) & 15u))
+    return fail(MOE_B200_ERR_ARG, "ep: out_shard must be a 16-byte aligned pointer");
+  for (int r = 0; r < N; ++r)
+    if (!ep->recv[r] || !ep->signal[r] || (reinterpret_cast<uintptr_t>(ep->recv[r]) & 15u))
+      return fail(MOE_B200_ERR_ARG, "ep: recv[r] (16-byte aligned) and signal[r] are required for every rank");
+  moe_b200_args a2 = *a;
+  a2.output = static_cast<uint16_t*>(ep->out_shard);   // passes the argument check; rows go through the map
+  const int phase = static_cast<int>(ep->epoch & 1u);
+  const size_t slot = static_cast<size_t>(ep->shard_tokens) * moe::kH;   // bf16 elements
+  moe::OutMap om{};
+  for (int r = 0; r < N; ++r)
+    om.base[r] = static_cast<uint16_t*>(ep->recv[r]) + static_cast<size_t>(phase) * N * slot;
+  om.shard = ep->shard_tokens;
+  om.slot_rows = ep->rank * ep->shard_tokens;
+  int rc = forward_impl(&a2, workspace, ws_bytes, stream, nullptr, nullptr, nullptr, &om);
+  if (rc) return rc;
+  moe::Layout L;
+  moe::compute_layout(T, a->num_local_experts, &L);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  moe::EpArgs e{};
+  for (int r = 0; r < N; ++r) e.signal[r] = ep->signal[r];
+  e.recv = static_cast<const uint16_t*>(ep->recv[ep->rank]) + static_cast<size_t>(phase) * N * slot;
+  e.out = static_cast<uint16_t*>(ep->out_shard);
+  e.world = N;
+  e.rank = ep->rank;
+  e.shard = ep->shard_tokens;
+  e.phase = phase;
+  e.epoch = ep->epoch;
+  e.status = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + L.status);
+  int launches = 0;
+  cudaError_t ce = moe::ep_finish_launch(e, device_info(dev).sms, static_cast<cudaStream_t>(stream), &launches);
+  g_last_launches += launches;
+  if (ce != cudaSuccess) return cuda_fail(ce, "ep signal / reduce launch");
+  return MOE_B200_OK;
 }
 
 moe_b200_timer* moe_b200_timer_create(void) { return new moe_b200_timer(); }

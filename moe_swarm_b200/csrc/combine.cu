@@ -19,7 +19,7 @@ static_assert(kCombineChunks * kCombineThreads * 4 == kH, "a row is a whole numb
 // row's chunks spread over seven SMs.
 
 __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const int* tok_nloc, const int* tok_rows,
-                                                                  const float* part2, uint16_t* out, int T,
+                                                                  const float* part2, OutMap out, int T,
                                                                   unsigned long long* trace) {
   MOE_TRACE_CTA(trace, 0);
   pdl_wait();   // the partial rows come from GEMM2
@@ -30,7 +30,7 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const int* tok
     const int kt = __ldg(tok_nloc + t);
     if (kt == 1) continue;
     if (kt == 0) {   // no local expert: this thread's 4 bf16 of the zero row
-      reinterpret_cast<uint2*>(out + static_cast<size_t>(t) * kH)[v] = make_uint2(0, 0);
+      reinterpret_cast<uint2*>(out_row(out, t))[v] = make_uint2(0, 0);
       continue;
     }
     int rows[kTopK];
@@ -52,7 +52,7 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const int* tok
         }
       __nv_bfloat162 lo = __floats2bfloat162_rn(s.x, s.y), hi = __floats2bfloat162_rn(s.z, s.w);
       uint2 pk = make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
-      *reinterpret_cast<uint2*>(out + static_cast<size_t>(t) * kH + 4 * v) = pk;
+      *reinterpret_cast<uint2*>(out_row(out, t) + 4 * v) = pk;
     }
   }
   (void)trace;
@@ -61,7 +61,7 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const int* tok
 
 // Launched as a programmatic dependent of GEMM2.
 cudaError_t combine_launch(int T, int grid, cudaStream_t st, const int* tok_nloc, const int* tok_rows,
-                           const float* part2, uint16_t* out, unsigned long long* trace) {
+                           const float* part2, const OutMap& out, unsigned long long* trace) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kCombineThreads);

@@ -8,6 +8,32 @@
 
 namespace moe {
 
+// Where token t's bf16 output row goes: the caller's output (shard == 0), or -- expert
+// parallelism over peer memory -- the receive buffer of the rank that owns t (owner t / shard),
+// at this rank's slot, so the row crosses NVLink from the epilogue that produces it.
+constexpr int kMaxRanks = 8;
+struct OutMap {
+  uint16_t* base[kMaxRanks];   // [0]: the output; EP: each rank's receive buffer (this call's phase)
+  int shard;                   // tokens per rank; 0: a single output
+  int slot_rows;               // EP: this rank's slot, rank * shard rows into each receive buffer
+};
+
+__host__ __device__ __forceinline__ uint16_t* out_row(const OutMap& m, int t) {
+  if (m.shard == 0) return m.base[0] + static_cast<size_t>(t) * kH;
+  const int r = t / m.shard;
+  return m.base[r] + (static_cast<size_t>(m.slot_rows) + (t - r * m.shard)) * kH;
+}
+
+// The end of an expert-parallel call over peer memory (ep.cu).
+struct EpArgs {
+  unsigned int* signal[kMaxRanks];   // per rank: its flag words [2][kMaxRanks] (peer-mapped)
+  const uint16_t* recv;              // this rank's receive buffer, this call's phase: [N][shard][kH]
+  uint16_t* out;                     // this rank's shard [shard][kH]
+  int world, rank, shard, phase;
+  unsigned int epoch;
+  int* status;
+};
+
 struct RouteArgs {
   const float* logits;
   const uint16_t* bias;
@@ -80,7 +106,7 @@ struct TileArgs {
   const int* tok_nloc;
   const int* tok_rows;
   float* part2;
-  uint16_t* out;
+  OutMap out;
   int* status;
   unsigned long long* trace;   // [kMaxSms][kTraceSlots] of this kernel (written by MOE_TRACE builds)
 };

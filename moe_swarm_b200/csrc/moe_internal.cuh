@@ -40,6 +40,7 @@ enum : int {
   kStWaitEpilogue = 0x104,
   kStWaitDrain = 0x105,
   kStWaitFixup = 0x106,   // a split tile's finisher waiting for the other contributors
+  kStWaitPeers = 0x107,   // expert parallelism: waiting for the other ranks' rows (ep.cu)
 };
 
 // Written by the routing scan, read by the GEMM kernels.

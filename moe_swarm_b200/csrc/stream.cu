@@ -335,7 +335,7 @@ __device__ void s_epi2(StreamSmem<2>& sm, const TileArgs& g, const STile& s, con
     if (c >= s.nr) break;
     const float v = __fmul_rn(acc[c], sm.col_w[par][c]);
     if (sm.col_k[par][c] == 1)
-      g.out[static_cast<size_t>(sm.col_t[par][c]) * kH + f] = bf16_bits(v);
+      out_row(g.out, sm.col_t[par][c])[f] = bf16_bits(v);
     else
       g.part2[static_cast<size_t>(s.row0 + c) * kH + f] = v;
   }

@@ -345,7 +345,7 @@ __device__ __forceinline__ void w_epi2(WideSmem<2>& sm, const TileArgs& g, const
         const int tv = sm.mt[ew][r];
         const int col = col0 + 16 * rd + 4 * ch;
         if (tv < 0) {
-          *reinterpret_cast<uint2*>(g.out + static_cast<size_t>(-1 - tv) * kH + col) =
+          *reinterpret_cast<uint2*>(out_row(g.out, -1 - tv) + col) =
               make_uint2(bf16x2_bits(v.x, v.y), bf16x2_bits(v.z, v.w));
         } else {
           *reinterpret_cast<float4*>(g.part2 + static_cast<size_t>(s.row0 + 32 * q + r) * kH + col) = v;

@@ -9,6 +9,11 @@ and logits are replicated, and the bf16 partial outputs are combined over NCCL -
 reduce-scatter (rank r keeps token rows [r*T/N, (r+1)*T/N), the input layout of a following
 sequence-sharded layer) or by all-reduce (every rank keeps all rows).
 
+`forward(..., combine="peer")` keeps the reduce-scatter's result layout but has no separate
+collective: the layer's GEMM2 and combine epilogues store each output row straight into the
+receive buffer of the rank that owns the row, over NVLink, and each rank sums the N slots of its
+rows in rank order (`moe_b200_forward_ep`; buffers in torch symmetric memory).
+
 `forward_dispatch` is the token-dispatch form a deployment uses when each rank owns its own
 tokens: a rank routes its tokens, sends each one only to the ranks holding its experts
 (all-to-all), computes the tokens it received with the pre-routed layer on its experts, and
@@ -23,6 +28,7 @@ import torch
 import torch.distributed as dist
 
 E_GLOBAL = 256
+H = 7168
 
 
 @dataclass(frozen=True)
@@ -65,6 +71,26 @@ def _default_route(routing_logits, routing_bias, routed_scaling_factor, like):
     return r["topk_idx"].clone(), r["topk_w"].clone()   # copies: route() returns workspace views
 
 
+class _PeerBuffers:
+    """Receive buffers and flag words of the peer-memory combine, mapped on every rank of the
+    group (torch symmetric memory): recv bf16 [2][N][tokens/N][7168], flags uint32 [2][8]
+    (zeroed before any rank signals).  Creating them is collective."""
+
+    def __init__(self, group, world: int, tokens: int, device):
+        import torch.distributed._symmetric_memory as symm
+        name = (group or dist.group.WORLD).group_name
+        self.tokens = tokens
+        self.recv = symm.empty(2 * world * (tokens // world) * H, dtype=torch.bfloat16, device=device)
+        self.flags = symm.empty(2 * 8, dtype=torch.int32, device=device)
+        self.flags.zero_()
+        self._handles = (symm.rendezvous(self.recv, name), symm.rendezvous(self.flags, name))
+        self.recv_ptrs = [int(p) for p in self._handles[0].buffer_ptrs]
+        self.flag_ptrs = [int(p) for p in self._handles[1].buffer_ptrs]
+        torch.cuda.synchronize(device)
+        dist.barrier(group)
+        self.epoch = 0
+
+
 class ExpertParallelMoE:
     """The layer on one rank of an expert-parallel group.
 
@@ -87,6 +113,7 @@ class ExpertParallelMoE:
             from . import run_routed as local_routed
         self.local_routed = local_routed
         self.route_fn = route_fn or _default_route
+        self._peer = None
 
     def partial(self, routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
                 gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, routed_scaling_factor):
@@ -99,7 +126,10 @@ class ExpertParallelMoE:
 
     def forward(self, *args, combine: str = "reduce_scatter", out: torch.Tensor | None = None):
         """Partial layer on this rank, then the combine: "reduce_scatter" returns this rank's
-        T/N rows of the full layer output, "all_reduce" returns all T rows."""
+        T/N rows of the full layer output, "all_reduce" returns all T rows, "peer" returns the
+        same rows as "reduce_scatter" with the combine done over peer memory inside the call."""
+        if combine == "peer":
+            return self._forward_peer(*args, out=out)
         part = self.partial(*args)
         if self.world == 1:
             return part
@@ -113,6 +143,46 @@ class ExpertParallelMoE:
         if out is None:
             out = torch.empty((hi - lo,) + tuple(part.shape[1:]), dtype=part.dtype, device=part.device)
         dist.reduce_scatter_tensor(out, part, group=self.group)
+        return out
+
+    def _forward_peer(self, routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
+                      gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, routed_scaling_factor, out=None):
+        import ctypes
+
+        from . import _args, _native, _validate, _workspace
+        T, E, dev = _validate(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
+                              gemm1_weights_scale, gemm2_weights, gemm2_weights_scale)
+        if E != self.shard.experts:
+            raise ValueError(f"rank {self.rank} holds {self.shard.experts} experts, got weights for {E}")
+        if T % self.world:
+            raise ValueError(f"the peer combine needs T divisible by {self.world}, got T={T}")
+        if self._peer is None or self._peer.tokens < T:
+            self._peer = _PeerBuffers(self.group, self.world, T, dev)
+        pb = self._peer
+        pb.epoch += 1
+        rows = T // self.world
+        if out is None:
+            out = torch.empty((rows, H), dtype=torch.bfloat16, device=dev)
+        elif not (out.dtype == torch.bfloat16 and tuple(out.shape) == (rows, H) and out.is_contiguous()
+                  and out.device == dev):
+            raise ValueError(f"out must be a contiguous bf16 [{rows}, {H}] tensor on {dev}")
+        if T == 0:
+            return out
+        ep = _native.MoeEp()
+        ep.world, ep.rank, ep.shard_tokens, ep.epoch = self.world, self.rank, rows, pb.epoch
+        for r in range(self.world):
+            ep.recv[r] = pb.recv_ptrs[r]
+            ep.signal[r] = pb.flag_ptrs[r]
+        ep.out_shard = out.data_ptr()
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        buf = _workspace(dev).get(T, E, stream)
+        a = _args(T, E, routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
+                  gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, self.shard.offset,
+                  routed_scaling_factor, out)
+        rc = _native.lib().moe_b200_forward_ep(ctypes.byref(a), ctypes.byref(ep), buf.data_ptr(), buf.numel(),
+                                               stream)
+        if rc != _native.OK:
+            raise RuntimeError(f"moe_b200_forward_ep failed ({rc}): {_native.last_error()}")
         return out
 
     def _exchange(self, send: torch.Tensor, send_counts, recv_counts) -> torch.Tensor:

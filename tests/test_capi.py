@@ -74,6 +74,38 @@ def test_forward_rejects_bad_arguments_without_touching_a_gpu():
     assert "aligned" in N.last_error()
 
 
+def test_forward_ep_rejects_bad_arguments_without_touching_a_gpu():
+    lib = N.lib()
+    a = _args(T=8)
+    for f in ("routing_logits", "routing_bias", "hidden_states", "hidden_states_scale", "gemm1_weights",
+              "gemm1_weights_scale", "gemm2_weights", "gemm2_weights_scale", "output"):
+        setattr(a, f, 1 << 20)
+
+    def ep(world=2, rank=0, shard=4, epoch=1, peers=2):
+        e = N.MoeEp()
+        e.world, e.rank, e.shard_tokens, e.epoch = world, rank, shard, epoch
+        for r in range(peers):
+            e.recv[r] = (1 << 21) * (r + 1)
+            e.signal[r] = (1 << 22) * (r + 1)
+        e.out_shard = 1 << 23
+        return e
+
+    def rc(e):
+        return lib.moe_b200_forward_ep(ctypes.byref(a), ctypes.byref(e), None, 0, None)
+
+    assert lib.moe_b200_forward_ep(ctypes.byref(a), None, None, 0, None) == N.ERR_ARG
+    assert rc(ep(world=0)) == N.ERR_ARG
+    assert rc(ep(world=9)) == N.ERR_ARG
+    assert rc(ep(rank=2)) == N.ERR_ARG
+    assert rc(ep(shard=3)) == N.ERR_ARG and "shard_tokens" in N.last_error()
+    assert rc(ep(epoch=0)) == N.ERR_ARG and "epoch" in N.last_error()
+    assert rc(ep(peers=1)) == N.ERR_ARG and "every rank" in N.last_error()
+    e = ep()
+    e.recv[1] = (1 << 21) + 4   # misaligned receive buffer
+    assert rc(e) == N.ERR_ARG
+    assert rc(ep()) == N.ERR_WORKSPACE   # valid EP arguments reach the workspace check
+
+
 def test_python_entry_validates_like_the_reference():
     T = 2
     x = {

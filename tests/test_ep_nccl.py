@@ -168,3 +168,68 @@ def test_two_rank_token_dispatch_matches_single_gpu(tmp_path):
         assert int(bad.sum()) <= 1e-3 * want.numel(), f"rank {rank}: {int(bad.sum())} elements outside tolerance"
         assert float(err.max()) <= 5 * C.ATOL
         assert want.abs().max() > 0
+
+
+PEER_TOKENS = (64, 640)   # the streaming kernels, then the wide ones
+
+
+def _peer_rank_main(rank, world, port, out_dir):
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    import moe_swarm_b200 as M
+    from moe_swarm_b200 import ep
+    from moe_swarm_b200 import workload as W
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    device = torch.device("cuda", rank)
+    torch.cuda.set_device(device)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                            device_id=device)
+    try:
+        sh = ep.shard(rank, world)
+        wts = W.make_weights_fast(sh.experts, 900 + rank, device=device)
+        layer = ep.ExpertParallelMoE()
+        res = {}
+        for t in PEER_TOKENS:
+            x = {k: v.to(device) for k, v in W.make_activations(t, 31 + t).items()}
+            args = (x["routing_logits"], x["routing_bias"], x["hidden_states"], x["hidden_states_scale"],
+                    wts["gemm1_weights"], wts["gemm1_weights_scale"], wts["gemm2_weights"],
+                    wts["gemm2_weights_scale"], 2.5)
+            rows = [layer.forward(*args, combine="peer").clone() for _ in range(3)]   # both phases, reuse
+            local = layer.partial(*args)
+            torch.cuda.synchronize()
+            res[t] = {"rows": [r.cpu() for r in rows], "local": local.cpu(),
+                      "status": M.device_status(device, t, sh.experts)}
+        torch.save(res, os.path.join(out_dir, f"peer{rank}.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_peer_combine_equals_sum_of_partials(tmp_path):
+    """The combine over peer memory (moe_b200_forward_ep): each rank's GEMM2 and combine
+    epilogues store its rows into the owning rank's buffer, and the owner sums the slots in rank
+    order.  Random routing (tokens with 0, 1 and several local experts) and random weights on
+    both ranks; T = 64 runs the streaming kernels, T = 640 the wide ones; three calls per size
+    cover both buffer phases and their reuse.  Every call's rows equal, bit for bit, the bf16
+    rounding of the fp32 sum of the two ranks' partial outputs (each computed by the plain
+    single-GPU call), and the device status stays 0."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    mp.start_processes(_peer_rank_main, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True,
+                       start_method="spawn")
+    parts = [torch.load(tmp_path / f"peer{r}.pt") for r in range(2)]
+    for t in PEER_TOKENS:
+        want = (parts[0][t]["local"].float() + parts[1][t]["local"].float()).to(torch.bfloat16)
+        assert want.float().abs().max() > 0
+        for r in range(2):
+            p = parts[r][t]
+            assert p["status"] == 0, f"rank {r} T={t}: device status {p['status']:#x}"
+            lo, hi = r * t // 2, (r + 1) * t // 2
+            for i, got in enumerate(p["rows"]):
+                assert torch.equal(got.view(torch.int16), want[lo:hi].view(torch.int16)), (r, t, i)
