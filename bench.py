@@ -524,6 +524,20 @@ def main():
             return shard
         return out
 
+    if peer:
+        # the peer buffers are created on the first call (collective); if this process cannot map
+        # peer memory, every rank falls back to the NCCL reduce-scatter and the line says so
+        try:
+            step(x, False)
+            ok = torch.ones(1, device=device)
+        except Exception as exc:   # noqa: BLE001 -- reported in the line
+            print(f"rank {rank}: peer-memory combine unavailable ({exc}); using the NCCL reduce-scatter",
+                  file=sys.stderr, flush=True)
+            ok = torch.zeros(1, device=device)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        if float(ok) < 1:
+            peer = False
+            config["combine"] = "nccl reduce_scatter bf16 (peer-memory combine unavailable on this box)"
     clocks = ClockSampler(device)
     if rank == 0:
         clocks.start()
@@ -547,6 +561,9 @@ def main():
         dist.barrier()
     torch.cuda.synchronize()
     ms = start.elapsed_time(end)
+    status = M.device_status(device, T, E_GLOBAL // world)
+    if status:
+        raise RuntimeError(f"rank {rank}: device status {status:#x} after the timed steps (a bounded wait gave up)")
     if peer:   # stage split of the same layer without the combine (untimed for the line's value)
         for _ in range(steps):
             timer.run(x)
