@@ -156,18 +156,18 @@ class ExpertParallelMoE:
             raise ValueError(f"rank {self.rank} holds {self.shard.experts} experts, got weights for {E}")
         if T % self.world:
             raise ValueError(f"the peer combine needs T divisible by {self.world}, got T={T}")
-        if self._peer is None or self._peer.tokens < T:
-            self._peer = _PeerBuffers(self.group, self.world, T, dev)
-        pb = self._peer
-        pb.epoch += 1
         rows = T // self.world
         if out is None:
             out = torch.empty((rows, H), dtype=torch.bfloat16, device=dev)
         elif not (out.dtype == torch.bfloat16 and tuple(out.shape) == (rows, H) and out.is_contiguous()
                   and out.device == dev):
             raise ValueError(f"out must be a contiguous bf16 [{rows}, {H}] tensor on {dev}")
-        if T == 0:
+        if T == 0:   # the same T on every rank: all skip together
             return out
+        if self._peer is None or self._peer.tokens < T:
+            self._peer = _PeerBuffers(self.group, self.world, T, dev)
+        pb = self._peer
+        pb.epoch += 1
         ep = _native.MoeEp()
         ep.world, ep.rank, ep.shard_tokens, ep.epoch = self.world, self.rank, rows, pb.epoch
         for r in range(self.world):
