@@ -585,8 +585,9 @@ cudaError_t route_launch(const RouteArgs& a, cudaStream_t st, int* launches) {
 // ---------------------------------------------------------------------------------------
 // Routing without a caller-provided workspace (moe_b200_route_noalloc).
 //
-// Its scratch -- the per-token pick lists, chunk counts, segment tables and plan -- lives in
-// this file-scope array, sized for kNoAllocMaxT tokens and 256 local experts.  Every GPU that
+// Its scratch -- the per-token local pick counts and row lists, the segment tables and the plan
+// -- lives in this file-scope array, sized for kNoAllocMaxT tokens and 256 local experts (the
+// pick lists and chunk counts stay in the routing CTA's shared memory).  Every GPU that
 // loads the library holds these bytes until the process exits, and every call on a device
 // reuses the same bytes: calls that overlap on the GPU (two streams, or two host threads on
 // one device) race on them and must be serialised by the caller.
