@@ -8,9 +8,10 @@
 // ranges, CTA c owning [w0(c), w0(c+1)) with w0(c) = floor(c*W/G), so every CTA streams the
 // same number of K-blocks (+-1) whatever the tile count.  In the decode regime, where the
 // routed experts give fewer tiles than SMs, everything is stream-K and all 148 SMs stream
-// weights.  A tile split across CTAs is finished by its last contributor (wide kernels and
-// streaming GEMM2) or, for streaming GEMM1, by stream_fin1_kernel after the GEMM; either sums
-// the partial accumulators of the contributing CTAs in CTA order (deterministic).  Only a CTA's
+// weights.  A tile split across CTAs is finished by its last contributor to arrive (wide
+// kernels), by its first contributor, which in this order reaches it last (streaming GEMM2), or
+// by stream_fin1_kernel after the GEMM (streaming GEMM1); each sums the partial accumulators of
+// the contributing CTAs in CTA order (deterministic).  Only a CTA's
 // first and last stream-K tile can be partial, so each CTA owns two partial slots: 2c (its
 // first) and 2c+1 (its last).
 #pragma once
