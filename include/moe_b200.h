@@ -168,6 +168,10 @@ typedef struct moe_b200_ep {
   void* recv[MOE_B200_MAX_RANKS];         /* per rank: its receive buffer */
   uint32_t* signal[MOE_B200_MAX_RANKS];   /* per rank: its flag words */
   void* out_shard;                        /* this rank's result, bf16 [shard_tokens][7168] */
+  uint32_t wait_limit_us;                 /* bound of the wait for the peers' rows in
+                                             microseconds; 0 selects the default, 2 s.  When it
+                                             runs out the call's kernels return and the device
+                                             status reads 0x107 (moe_b200_device_status). */
 } moe_b200_ep;
 MOE_B200_API int moe_b200_forward_ep(const moe_b200_args* args, const moe_b200_ep* ep, void* workspace,
                                      size_t workspace_bytes, void* stream);
@@ -190,7 +194,10 @@ MOE_B200_API int moe_b200_route(const moe_b200_args* args, void* workspace, size
  *     a workspace); num_local_experts <= 256;
  *   - every call on a device shares that array: calls that overlap on the GPU (two streams or
  *     two host threads on one device) race and must be serialised by the caller;
- *   - the first call on a device looks up the array's device address (once per device).
+ *   - the first call on a device looks up the array's device address (once per device, with
+ *     that device current) and keeps it for the life of the process; a cudaDeviceReset of that
+ *     device in the calling process invalidates the kept address, so make no call on a device
+ *     after resetting it;
  * Only routing_logits, routing_bias, num_tokens, num_local_experts, local_expert_offset and
  * routed_scaling_factor of `args` are read.  Outputs (device memory, caller-allocated):
  *   topk_idx      int32 [T, 8]  selected global experts, ascending per token

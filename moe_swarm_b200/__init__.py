@@ -43,7 +43,7 @@ def _check(cond: bool, msg: str):
 
 
 class Workspace:
-    """Per-device scratch reused across calls (never results: every call recomputes).
+    """Scratch of one (device, stream) reused across calls (never results: every call recomputes).
 
     Grows to the largest (T, E_local) seen; the self-resetting counters are zeroed
     whenever the layout changes.
@@ -72,15 +72,22 @@ class Workspace:
 
 
 _ws_lock = threading.Lock()
-_workspaces: dict[int, Workspace] = {}
+_workspaces: dict[tuple[int, int], Workspace] = {}
 
 
-def _workspace(device: torch.device) -> Workspace:
+def _workspace(device: torch.device, stream: int | None = None) -> Workspace:
+    """The workspace of (device, stream).  Calls on one stream run one after another on the GPU
+    and may share scratch; calls on two streams may overlap on the GPU, so each stream gets its
+    own (a shared one would let them race on the same counters and permuted rows).  ``stream`` is
+    the raw ``cudaStream_t`` value; None means the device's current stream."""
     idx = device.index if device.index is not None else torch.cuda.current_device()
+    if stream is None:
+        stream = torch.cuda.current_stream(torch.device("cuda", idx)).cuda_stream
+    key = (idx, int(stream))
     with _ws_lock:
-        ws = _workspaces.get(idx)
+        ws = _workspaces.get(key)
         if ws is None:
-            ws = _workspaces[idx] = Workspace(torch.device("cuda", idx))
+            ws = _workspaces[key] = Workspace(torch.device("cuda", idx))
         return ws
 
 
@@ -139,6 +146,11 @@ def run(routing_logits: torch.Tensor, routing_bias: torch.Tensor, hidden_states:
     ``[local_expert_offset, local_expert_offset + E_local)`` are computed; the result is
     this rank's partial sum (``reference/kernel_pytorch_v1.py:126-130``).
     ``out`` (optional, bf16 ``[T, 7168]``) receives the result instead of a new tensor.
+
+    The call is enqueued on the current CUDA stream without a host synchronisation.  Its scratch
+    is a workspace kept per (device, stream): calls on different streams of one device may run
+    concurrently on the GPU, each with its own scratch.  Calls on one stream from several host
+    threads share that stream's workspace, which is safe because the GPU runs them in stream order.
     """
     T, E, dev = _validate(routing_logits, routing_bias, hidden_states, hidden_states_scale,
                           gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale)
@@ -150,7 +162,7 @@ def run(routing_logits: torch.Tensor, routing_bias: torch.Tensor, hidden_states:
     if T == 0:
         return out
     stream = torch.cuda.current_stream(dev).cuda_stream
-    buf = _workspace(dev).get(T, E, stream)
+    buf = _workspace(dev, stream).get(T, E, stream)
     a = _args(T, E, routing_logits, routing_bias, hidden_states, hidden_states_scale,
               gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale,
               local_expert_offset, routed_scaling_factor, out)
@@ -191,7 +203,7 @@ def run_routed(topk_idx: torch.Tensor, topk_w: torch.Tensor, hidden_states: torc
     if T == 0:
         return out
     stream = torch.cuda.current_stream(dev).cuda_stream
-    buf = _workspace(dev).get(T, E, stream)
+    buf = _workspace(dev, stream).get(T, E, stream)
     a = _args(T, E, dummy_logits, dummy_bias, hidden_states, hidden_states_scale, gemm1_weights,
               gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_expert_offset, 1.0, out)
     a.routing_logits = None
@@ -262,7 +274,7 @@ def route(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm
     if out is None:
         out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
     stream = torch.cuda.current_stream(dev).cuda_stream
-    buf = _workspace(dev).get(T, E, stream)
+    buf = _workspace(dev, stream).get(T, E, stream)
     a = _args(T, E, routing_logits, routing_bias, hidden_states, hidden_states_scale,
               gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale,
               local_expert_offset, routed_scaling_factor, out)
@@ -298,7 +310,7 @@ def read_routing(buf: torch.Tensor, T: int, E: int) -> dict:
 def read_intermediate(device, T: int, E: int) -> dict:
     """The GEMM1 output (hi/lo e4m3 pair and scales) left in the device's workspace by
     the last call with these sizes: c_hi/c_lo uint8 [R, 2048], c_scale f32 [16, R]."""
-    buf = _workspace(torch.device(device)).buf
+    buf = _workspace(torch.device(device)).buf   # the current stream's workspace
     L = _native.layout(T, E)
     plan = buf[L.plan:L.plan + 64].view(torch.int32)
     R = int(plan[2].item())
@@ -312,7 +324,7 @@ def device_status(device=None, T: int | None = None, E: int | None = None, clear
     """Synchronises and returns the device status word of the device's workspace
     (0 = ok; otherwise the code of a bounded device-side wait that gave up)."""
     dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
-    ws = _workspace(dev)
+    ws = _workspace(dev)   # the current stream's workspace
     if ws.buf is None:
         return 0
     T0, E0 = ws.key if T is None else (T, E)

@@ -70,6 +70,7 @@ class MoeEp(ctypes.Structure):
         ("recv", ctypes.c_void_p * MAX_RANKS),
         ("signal", ctypes.c_void_p * MAX_RANKS),
         ("out_shard", ctypes.c_void_p),
+        ("wait_limit_us", ctypes.c_uint32),
     ]
 
 

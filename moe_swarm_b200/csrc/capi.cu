@@ -457,6 +457,7 @@ int moe_b200_forward_ep(const moe_b200_args* a, const moe_b200_ep* ep, void* wor
   e.shard = ep->shard_tokens;
   e.phase = phase;
   e.epoch = ep->epoch;
+  e.wait_ns = ep->wait_limit_us ? static_cast<unsigned long long>(ep->wait_limit_us) * 1000ull : moe::kWaitLimitNs;
   e.status = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + L.status);
   int launches = 0;
   cudaError_t ce = moe::ep_finish_launch(e, device_info(dev).sms, static_cast<cudaStream_t>(stream), &launches);

@@ -10,7 +10,7 @@
 //   ep_signal_kernel  after the layer's kernels (stream order: their stores have been
 //                     performed), a system-scope fence, then lane r stores this call's epoch
 //                     into rank r's flag [phase][this rank] with release semantics.
-//   ep_reduce_kernel  waits (bounded) until all N flags of this rank's phase read this epoch,
+//   ep_reduce_kernel  waits (bounded by EpArgs::wait_ns) until all N flags of this rank's phase read this epoch,
 //                     then sums the N slots row by row in rank order (fp32, one bf16 rounding)
 //                     into this rank's shard.
 //
@@ -52,7 +52,7 @@ __global__ void __launch_bounds__(kEpThreads) ep_reduce_kernel(EpArgs a) {
     int ok = 1;
     for (int j = 0; j < a.world && ok; ++j) {
       for (uint32_t i = 0; ld_acquire_sys(flags + j) != a.epoch; ++i) {
-        if ((i & 63u) == 63u && globaltimer_ns() - t0 > kWaitLimitNs) {
+        if ((i & 63u) == 63u && globaltimer_ns() - t0 > a.wait_ns) {
           atomicCAS(a.status, 0, kStWaitPeers);
           ok = 0;
           break;

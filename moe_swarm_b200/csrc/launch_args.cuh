@@ -31,6 +31,7 @@ struct EpArgs {
   uint16_t* out;                     // this rank's shard [shard][kH]
   int world, rank, shard, phase;
   unsigned int epoch;
+  unsigned long long wait_ns;        // bound of the wait for the peers' flags
   int* status;
 };
 

@@ -31,6 +31,11 @@ constexpr int kTraceSlots = 16;   // per-CTA counters of a traced build (MOE_TRA
 constexpr int kTraceKernels = 8;  // stream GEMM1, stream GEMM2, wide GEMM1, wide GEMM2, routing,
                                   // scatter, GEMM1 finalize, combine
 
+// Bound of every device-side wait (mbarrier phases, stream-K arrivals, peer flags): far above
+// any legitimate stall.  The peer-flag wait of expert parallelism takes a caller-given bound
+// instead when one is passed (moe_b200_ep::wait_limit_us).
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;   // 2 s
+
 // Device status codes (first one wins).
 enum : int {
   kStOk = 0,

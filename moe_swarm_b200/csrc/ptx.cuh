@@ -11,9 +11,10 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include "moe_internal.cuh"
+
 namespace moe {
 
-constexpr uint64_t kWaitLimitNs = 2000000000ull;   // 2 s: far above any legitimate stall
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -132,42 +133,6 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
                ::"r"(smem_u32(bar)) : "memory");
 }
 
-// Two loads of 32 lanes x 16 consecutive 32-bit columns (lane i of the warp reads TMEM
-// lane base_lane+i), then tcgen05.wait::ld.  The wait names every destination register
-// as an in/out operand so no use of a loaded value can be scheduled above it.
-__device__ __forceinline__ void tmem_ld16x2_wait(uint32_t ta, uint32_t tb, float* a, float* b) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
-        "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(ta));
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
-        "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),
-        "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(tb));
-  asm volatile(
-      "tcgen05.wait::ld.sync.aligned;"
-      : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),
-        "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]),
-        "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]),
-        "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]),
-        "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]),
-        "+r"(r[31])
-      :
-      : "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    a[i] = __uint_as_float(r[i]);
-    b[i] = __uint_as_float(r[16 + i]);
-  }
-}
-
 // Issue only: two loads of 32 lanes x 16 consecutive 32-bit columns, at TMEM addresses ta
 // (into r[0..15]) and tb (into r[16..31]).  The registers hold the data only after
 // tmem_wait_ld32(r); a load issued after that wait overlaps whatever runs before the next one.
@@ -226,17 +191,6 @@ __device__ __forceinline__ void tmem_ld32x2_wait(uint32_t ta, uint32_t tb, float
     a[i] = __uint_as_float(r[i]);
     b[i] = __uint_as_float(r[32 + i]);
   }
-}
-
-// 2-D tiled load of four gathered rows (tile::gather4): rows y0..y3 at column x.
-__device__ __forceinline__ void tma_gather4(void* dst, const CUtensorMap* m, uint64_t* bar, int32_t x,
-                                            int32_t y0, int32_t y1, int32_t y2, int32_t y3) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];"
-      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(bar)), "r"(x),
-        "r"(y0), "r"(y1), "r"(y2), "r"(y3)
-      : "memory");
 }
 
 // Instruction descriptor, kind::f8f6f4: D f32, A/B e4m3, both K-major, M x N.

@@ -207,7 +207,7 @@ __device__ __forceinline__ void w_mma(WideSmem<MODE>& sm, uint32_t tmem, const T
   constexpr int ST = WCfg<MODE>::STAGES;
   constexpr uint32_t idesc = idesc_e4m3_f32(128, 256);
   uint32_t stage = 0, phase = 0, tk = 0, buf = 0;
-  long long tw_t = 0, tw_f = 0, t_first = 0;
+  long long tw_t = 0, tw_f = 0, t_first = 0, t_iss = 0;
   SegIter it(sk, blockIdx.x);
   int tile, k0, k1;
   while (it.next(tile, k0, k1)) {
@@ -223,6 +223,7 @@ __device__ __forceinline__ void w_mma(WideSmem<MODE>& sm, uint32_t tmem, const T
       if (t_first == 0) t_first = static_cast<long long>(globaltimer_ns());
 #endif
       tc_fence_after();
+      t0 = MOE_WCLK();
       {
         const uint32_t st = smem_u32(sm.stage[stage]);
         const uint32_t d = tmem + buf * 256u;
@@ -240,6 +241,7 @@ __device__ __forceinline__ void w_mma(WideSmem<MODE>& sm, uint32_t tmem, const T
       }
       mma_commit(&sm.empty[stage]);
       mma_commit(&sm.tfull[buf]);
+      MOE_WADD(t_iss, t0);
       tk ^= 1u << buf;
       buf ^= 1u;
       if (++stage == ST) {
@@ -256,6 +258,7 @@ done:
   g.trace[blockIdx.x * kTraceSlots + 4] = tw_f;
   g.trace[blockIdx.x * kTraceSlots + 5] = tw_t;
   g.trace[blockIdx.x * kTraceSlots + 11] = t_first;
+  g.trace[blockIdx.x * kTraceSlots + 14] = t_iss;
 #endif
 }
 
@@ -562,6 +565,7 @@ __device__ __forceinline__ void w_epilogue(WideSmem<MODE>& sm, uint32_t tmem, co
     tr[8] = te;
     tr[9] = tf;
     tr[10] = ts;
+    tr[13] = clock64();
     tr[1] = globaltimer_ns();
   }
 #endif
@@ -613,7 +617,10 @@ __global__ void __launch_bounds__(kWThreads, 1)
   __syncthreads();
   tc_fence_after();
 #ifdef MOE_TRACE
-  if (threadIdx.x == 0) g.trace[blockIdx.x * kTraceSlots + 0] = globaltimer_ns();
+  if (threadIdx.x == 0) {
+    g.trace[blockIdx.x * kTraceSlots + 0] = globaltimer_ns();
+    g.trace[blockIdx.x * kTraceSlots + 12] = clock64();
+  }
 #endif
   const uint32_t tmem = sm.tmem_base;
   // 384 threads x 168 registers at launch = 128 x 56 (producer/MMA warpgroup) + 256 x 224

@@ -175,7 +175,7 @@ class ExpertParallelMoE:
             ep.signal[r] = pb.flag_ptrs[r]
         ep.out_shard = out.data_ptr()
         stream = torch.cuda.current_stream(dev).cuda_stream
-        buf = _workspace(dev).get(T, E, stream)
+        buf = _workspace(dev, stream).get(T, E, stream)
         a = _args(T, E, routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
                   gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, self.shard.offset,
                   routed_scaling_factor, out)

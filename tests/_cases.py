@@ -82,3 +82,60 @@ def make_case(T, seed, E_local=32, offset=0, skew=0.0, rsf=2.5, fill_missing_nan
 
 def to_device(x, device):
     return {k: (v.to(device) if isinstance(v, torch.Tensor) else v) for k, v in x.items()}
+
+
+class DeviceExperts:
+    """A stacked weight tensor on the GPU that the CPU oracle indexes one expert at a time: ``[le]``
+    copies only that expert to the host, so the oracle of a large configuration materialises on the
+    CPU just the experts its sampled tokens are routed to."""
+
+    def __init__(self, t):
+        self.t = t
+        self.shape = tuple(t.shape)
+
+    def __getitem__(self, le):
+        return self.t[le].cpu()
+
+
+def sample_tokens(idx, w, offset, E_local, T, limit=24, seed=0):
+    """Tokens whose rows exercise the edges of the large-batch path: the first and last rows of the
+    128-row token tiles of the most, least and median loaded local experts, tokens with the most
+    local experts, tokens with none, and the first and last token."""
+    tok, le, _, counts = O.local_permutation(idx, w, offset, E_local)
+    starts = torch.cumsum(counts, 0) - counts
+    nloc = torch.bincount(tok, minlength=T)
+    picks = []
+    live = (counts > 0).nonzero().flatten()
+    if len(live):
+        order = live[torch.argsort(counts[live], stable=True)]
+        for e in (int(order[-1]), int(order[0]), int(order[len(order) // 2])):
+            n, s = int(counts[e]), int(starts[e])
+            for pos in (0, 127, 128, 255, 256, n - 1):
+                if 0 <= pos < n:
+                    picks.append(int(tok[s + pos]))
+    most = int(nloc.max())
+    picks += [int(t) for t in (nloc == most).nonzero().flatten()[:4]]
+    picks += [int(t) for t in (nloc == 0).nonzero().flatten()[:2]]
+    picks += [0, T - 1]
+    g = torch.Generator().manual_seed(seed)
+    picks += [int(t) for t in torch.randint(0, T, (4,), generator=g)]
+    out = []
+    for t in picks:
+        if t not in out:
+            out.append(t)
+    return torch.tensor(out[:limit], dtype=torch.long)
+
+
+def oracle_rows(act, dev_weights, tokens, offset, rsf=2.5):
+    """The oracle's output rows (spec/reference_official.py semantics, oracle/moe_ref.py) for the
+    given tokens only.  Every output row depends on its own token alone -- its routing, its
+    activations and its experts -- so the rows equal those of the whole-batch oracle."""
+    idx, w = O.route(act["routing_logits"], act["routing_bias"], rsf)
+    A = O.dequant_tokens(act["hidden_states"][tokens], act["hidden_states_scale"][:, tokens])
+    with torch.no_grad():
+        out = O._experts_fp32(A, idx[tokens], w[tokens],
+                              DeviceExperts(dev_weights["gemm1_weights"]),
+                              DeviceExperts(dev_weights["gemm1_weights_scale"]),
+                              DeviceExperts(dev_weights["gemm2_weights"]),
+                              DeviceExperts(dev_weights["gemm2_weights_scale"]), offset)
+    return out.to(torch.bfloat16)

@@ -166,3 +166,17 @@ def test_gemm2_operand_precision_choice():
     gap = (outs["pair"] - outs["pair16"]).abs().max()
     assert gap <= 1e-3 * outs["pair16"].abs().max(), f"unscaled residual moved an output by {gap}"
     assert bad["fp8"] > 0.05 * g["official"].numel()
+
+
+def test_sampled_oracle_rows_equal_whole_batch_rows():
+    """The large-configuration GPU tests evaluate the oracle on a token sample only; its rows must
+    be bit-identical to the same rows of the whole-batch oracle."""
+    x = C.make_case(40, 17, E_local=8, offset=0)
+    full = O.run(**x)
+    idx, w = O.route(x["routing_logits"], x["routing_bias"], 2.5)
+    tokens = C.sample_tokens(idx, w, 0, 8, 40, limit=12)
+    assert len(tokens) >= 4
+    act = {k: x[k] for k in ("routing_logits", "routing_bias", "hidden_states", "hidden_states_scale")}
+    weights = {k: x[k] for k in ("gemm1_weights", "gemm1_weights_scale", "gemm2_weights", "gemm2_weights_scale")}
+    rows = C.oracle_rows(act, weights, tokens, 0)
+    assert torch.equal(rows.view(torch.int16), full[tokens].view(torch.int16))

@@ -57,10 +57,11 @@ def _route_noalloc(x, E, offset, device):
     return outs
 
 
-@pytest.mark.parametrize("E,offset", [(32, 0), (64, 128)])
+@pytest.mark.parametrize("E,offset", [(32, 0), (64, 128), (256, 0)])
 def test_noalloc_routing_equals_workspace_routing_twice(cuda_device, E, offset):
     w = _weights(E, cuda_device)
-    for T, seed in ((48, 301), (200, 302)):   # two calls in a row on the shared scratch
+    # two calls in a row on the shared scratch, the second at the 256-token limit
+    for T, seed in ((48, 301), (256, 302)):
         x = {k: v.to(cuda_device) for k, v in W.make_activations(T, seed).items()}
         got = _route_noalloc(x, E, offset, cuda_device)
         ref = M.route(**x, **w, local_expert_offset=offset, routed_scaling_factor=2.5)
