@@ -236,7 +236,7 @@ class StageTimer:
         if out is None:
             out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
         stream = torch.cuda.current_stream(dev).cuda_stream
-        buf = M._workspace(dev).get(T, E, stream)
+        buf = M._workspace(dev, stream).get(T, E, stream)
         a = M._args(T, E, x["routing_logits"], x["routing_bias"], x["hidden_states"],
                     x["hidden_states_scale"], x["gemm1_weights"], x["gemm1_weights_scale"],
                     x["gemm2_weights"], x["gemm2_weights_scale"], x["local_expert_offset"],
