@@ -14,9 +14,17 @@ At N=1 the line also carries the single-GPU sweeps with 32 local experts: decode
 T in {1,7,16,32,64,80} (HBM-bound), mid-batch T=901 with skewed routing, and prefill
 T in {8192,16384} (tensor-bound), each timed per call after an L2 flush.
 
+The timed steps are plain layer calls (moe_swarm_b200.run, or the peer-memory EP layer); the
+per-stage split and the dominant kernel's launch time come from a separate loop of the same calls
+with CUDA events between the stages.  The line also carries the skewed-load variant of the
+workload (per-expert logit bias N(0, 0.5)).
+
 Inputs are synthetic (seeded, distributions of the benchmark configs); weights are
-random-init on the device.  `--impl reference` times the CPU oracle port of the
-reference's PyTorch kernel (reference/kernel_pytorch_v1.py) on the host cores.
+random-init on the device.  The CPU baseline (`cpu_baseline`, and each sweep record's) and
+`--impl reference` time the oracle port of the reference's PyTorch kernel
+(reference/kernel_pytorch_v1.py) on the host cores with all threads, on the whole workload: the
+256-expert layer as 8 reference calls of 32 local experts (offsets 0..224), measured, not
+extrapolated.
 """
 
 from __future__ import annotations
@@ -256,38 +264,68 @@ class StageTimer:
 
 
 # ----------------------------------------------------------------------------- CPU baseline
-def cpu_sample(act_cpu, world, seed=0, k_experts=8, reps=1):
-    """Times the oracle port of reference/kernel_pytorch_v1.kernel on the host cores for the
-    first k experts of rank 0's shard, and scales by routed rows to the whole workload."""
+SLICE_E = 32   # the reference's layer holds 32 local experts (spec/reference_official.py:44)
+
+
+def slice_weights_cpu(dev_weights, E=SLICE_E):
+    """Host copies of the first E experts of a device weight set: the operands of the CPU
+    reference calls.  The reference's work depends on the routed rows, not on the weight values,
+    so one 32-expert slice serves every offset."""
+    return {k: dev_weights[k][:E].cpu() for k in ("gemm1_weights", "gemm1_weights_scale", "gemm2_weights",
+                                                  "gemm2_weights_scale")}
+
+
+def cpu_ep_layer(act_cpu, w_cpu):
+    """One full EP workload on the host cores, measured (not extrapolated): the 256-expert layer as
+    the reference computes it, 8 calls of the oracle port of reference/kernel_pytorch_v1.kernel with
+    32 local experts each, at local_expert_offset 0, 32, ..., 224 (the reference's own EP convention,
+    reference/kernel_pytorch_v1.py:126-130); returns the summed seconds."""
     from oracle import moe_ref as O
-    import moe_swarm_b200.workload as W
+    x = dict(act_cpu)
+    x.update(w_cpu)
+    x["routed_scaling_factor"] = 2.5
+    t0 = time.perf_counter()
+    for off in range(0, E_GLOBAL, SLICE_E):
+        x["local_expert_offset"] = off
+        O.run_v1(**x)
+    return time.perf_counter() - t0
+
+
+def cpu_baseline_ep(act_cpu, w_cpu, steps=1):
+    """The EP workload timed on the host cores with all threads: one warm-up slice call, then
+    `steps` whole layers (8 slice calls each); the median layer time."""
+    from oracle import moe_ref as O
     torch.set_num_threads(os.cpu_count() or 1)
     T = act_cpu["routing_logits"].shape[0]
-    idx, w = O.route(act_cpu["routing_logits"], act_cpu["routing_bias"], 2.5)
-    total_rows = int(((idx >= 0) & (idx < E_GLOBAL)).sum())          # all 256 experts over all ranks
-    _, _, _, counts = O.local_permutation(idx, w, 0, E_GLOBAL)
-    # a contiguous block of k experts (a k-expert shard), the first one holding routed rows
-    lo = int((counts > 0).nonzero()[0]) if int(counts.sum()) else 0
-    lo = min(lo, E_GLOBAL - k_experts)
-    E = k_experts
     x = dict(act_cpu)
-    x.update(W.make_weights(E, lo, seed))
-    x["local_expert_offset"] = lo
+    x.update(w_cpu)
+    x["local_expert_offset"] = 0
     x["routed_scaling_factor"] = 2.5
-    sample_rows = int(sum(int(counts[e]) for e in range(lo, lo + E)))
-    O.run_v1(**x)                                                     # warm-up
-    best = None
-    for _ in range(reps):
+    O.run_v1(**x)   # warm-up (one 32-expert slice)
+    secs = sorted(cpu_ep_layer(act_cpu, w_cpu) for _ in range(steps))
+    med = secs[len(secs) // 2]
+    return {"value": T / med, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": (f"the whole workload, measured: oracle port of reference/kernel_pytorch_v1.kernel, "
+                       f"8 calls of 32 local experts at offsets 0..224 (T={T}), median of {steps} layer(s): "
+                       f"{med:.2f} s per layer; one 32-expert weight slice serves every offset"),
+            "seconds_per_layer": med, "layers": steps}
+
+
+def cpu_sweep_point(x_cpu, T):
+    """One call each of the oracle ports of reference/kernel_pytorch_v1.kernel and, for T <= 901,
+    spec/reference_official.run on the host cores, for a sweep configuration (seconds)."""
+    from oracle import moe_ref as O
+    torch.set_num_threads(os.cpu_count() or 1)
+    t0 = time.perf_counter()
+    O.run_v1(**x_cpu)
+    v1 = time.perf_counter() - t0
+    rec = {"v1_s": round(v1, 3), "v1_tokens_per_s": round(T / v1, 1), "cores": torch.get_num_threads(),
+           "kind": "port"}
+    if T <= 901:
         t0 = time.perf_counter()
-        O.run_v1(**x)
-        dt = time.perf_counter() - t0
-        best = dt if best is None else min(best, dt)
-    est = best * total_rows / max(1, sample_rows)
-    return {"value": T / est, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
-            "sample": (f"oracle port of reference/kernel_pytorch_v1.kernel on {E} local experts "
-                       f"[{lo},{lo + E}) holding {sample_rows} of {total_rows} routed rows at T={T}, "
-                       f"{best:.2f} s, scaled by routed rows to all 256 experts"),
-            "est_seconds_full": est}
+        O.run(**x_cpu)
+        rec["official_s"] = round(time.perf_counter() - t0, 3)
+    return rec
 
 
 # ----------------------------------------------------------------------------- sweeps (N=1)
@@ -330,18 +368,20 @@ def roofline_record(f, T, us, peaks_, fp8_peak):
 FP8_PEAK_SOURCE = "2x the measured cuBLAS bf16 burst peak (no measured fp8 peak)"
 
 
-def sweep(device, steps, peaks_):
+def sweep(device, steps, peaks_, cpu=True):
     import moe_swarm_b200 as M
     import moe_swarm_b200.workload as W
     out = []
     weights = W.make_weights_fast(32, 7, device=device)
+    w_cpu = slice_weights_cpu(weights) if cpu else None
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
     timer = StageTimer()
     fp8_peak = 2.0 * peaks_["bf16_tflops"]
     for name, T, skew in [("decode", 1, 0.0), ("decode", 7, 0.0), ("decode", 16, 0.0), ("decode", 32, 0.0),
                           ("decode", 64, 0.0), ("decode", 80, 0.0), ("mid_skewed", 901, 0.5),
                           ("prefill", 8192, 0.0), ("prefill", 16384, 0.0)]:
-        x = {k: v.to(device) for k, v in W.make_activations(T, 1000 + T, skew=skew).items()}
+        act = W.make_activations(T, 1000 + T if T != 1 else 1000, skew=skew)   # T=1: seed 1000 routes one local expert
+        x = {k: v.to(device) for k, v in act.items()}
         x.update(weights)
         x["local_expert_offset"] = 0
         x["routed_scaling_factor"] = 2.5
@@ -378,6 +418,12 @@ def sweep(device, steps, peaks_):
             rec["graph_us"] = round(gt[len(gt) // 2], 1)
             del g
         rec["stage_us"] = {k: round(v * 1e3 / calls, 1) for k, v in zip(("route", "gemm1", "gemm2"), stage_ms)}
+        if w_cpu is not None:
+            xc = dict(act)
+            xc.update(w_cpu)
+            xc["local_expert_offset"] = 0
+            xc["routed_scaling_factor"] = 2.5
+            rec["cpu_baseline"] = cpu_sweep_point(xc, T)
         out.append(rec)
         del x
     return out, {"fp8_peak_tflops": fp8_peak, "fp8_peak_source": FP8_PEAK_SOURCE}
@@ -429,6 +475,59 @@ def profile_case(args):
         raise SystemExit(1)
 
 
+def reference_arm(args, config):
+    """--impl reference: the reference's own CPU implementation of the layer (the oracle port of
+    reference/kernel_pytorch_v1.kernel; the reference is Python and cannot travel to the GPU box)
+    timed on this box's host cores with all threads, on the same workload, metric and unit as the
+    GPU arm.  A step is the whole T=4096, 256-expert layer: 8 reference calls of 32 local experts
+    (the reference's layer size) at offsets 0..224.  If K such steps would take longer than about
+    four minutes, a step is one of those calls instead, the offsets taken in turn, and the layer
+    time is 8 x the median call; the line says which."""
+    import moe_swarm_b200.workload as W
+    from oracle import moe_ref as O
+    torch.set_num_threads(os.cpu_count() or 1)
+    act = W.make_activations(EP_T, 0)
+    dev = torch.device("cuda", 0) if torch.cuda.is_available() else torch.device("cpu")
+    w_cpu = slice_weights_cpu(W.make_weights_fast(SLICE_E, 0, device=dev))
+    x = dict(act)
+    x.update(w_cpu)
+    x["routed_scaling_factor"] = 2.5
+    x["local_expert_offset"] = 0
+    t0 = time.perf_counter()
+    O.run_v1(**x)                      # warm-up: one 32-expert call
+    est_layer = 8 * (time.perf_counter() - t0)
+    steps = max(1, args.steps)
+    whole = steps * est_layer <= 240.0
+    per_step = []
+    for i in range(steps):
+        if whole:
+            per_step.append(cpu_ep_layer(act, w_cpu))
+        else:
+            x["local_expert_offset"] = SLICE_E * (i % 8)
+            t0 = time.perf_counter()
+            O.run_v1(**x)
+            per_step.append(time.perf_counter() - t0)
+    srt = sorted(per_step)
+    med = srt[len(srt) // 2]
+    layer_s = med if whole else 8 * med
+    value = EP_T / layer_s
+    sample = (f"oracle port of reference/kernel_pytorch_v1.kernel on {torch.get_num_threads()} threads; "
+              + (f"each step the whole layer: 8 calls of 32 local experts at offsets 0..224, median "
+                 f"{layer_s:.2f} s" if whole else
+                 f"each step one call of 32 local experts, offsets 0..224 in turn; layer = 8 x median call "
+                 f"= {layer_s:.2f} s"))
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": "tokens/s",
+            "n_gpus": args.gpus, "steps": steps, "warmup": 1,
+            "ms_per_step": round(med * 1e3, 1), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16 GEMMs, fp32 accumulate (CPU)",
+            "data": "synthetic", "config": dict(config, step=("whole layer" if whole else "one 32-expert call")),
+            "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": torch.get_num_threads(),
+                             "kind": "port", "sample": sample},
+            "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -439,7 +538,7 @@ def main():
     ap.add_argument("--ep-combine", choices=["peer", "nccl"], default="peer",
                     help="N > 1: combine over peer memory inside the layer call (moe_b200_forward_ep), "
                          "or the layer followed by an NCCL reduce-scatter")
-    ap.add_argument("--cpu-experts", type=int, default=8)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU reference baselines of the GPU arm")
     ap.add_argument("--workloads", default=None, metavar="FILE",
                     help="replay a flashinfer-bench workload file (jsonl): one JSON line per workload")
     ap.add_argument("--blob-root", default=None, help="directory the workload file's blob paths are relative to")
@@ -467,26 +566,7 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return
-        import moe_swarm_b200.workload as W
-        act = W.make_activations(EP_T, 0)
-        vals = []
-        for i in range(max(1, steps)):
-            c = cpu_sample(act, world, k_experts=args.cpu_experts, reps=1)
-            vals.append(c)
-            if i + 1 >= min(steps, 3):
-                break
-        vals.sort(key=lambda c: c["value"])
-        c = vals[len(vals) // 2]
-        line = {"impl": "reference", "metric": METRIC, "value": round(c["value"], 2), "unit": "tokens/s",
-                "n_gpus": args.gpus, "steps": len(vals), "warmup": 1,
-                "ms_per_step": round(c["est_seconds_full"] * 1e3, 1), "higher_is_better": True,
-                "scaling": "strong", "vs_baseline": None, "dtype": "bf16 (CPU)", "data": "synthetic",
-                "config": config,
-                "cpu_baseline": {k: c[k] for k in ("value", "unit", "cores", "kind", "sample")},
-                "e2e": {"value": round(c["value"], 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
-                        "d2h_bytes_per_step": 0}}
-        print(json.dumps(line), flush=True)
-        return
+        return reference_arm(args, config)
 
     import moe_swarm_b200 as M
     from moe_swarm_b200 import _native as N
@@ -515,8 +595,10 @@ def main():
                 inp["gemm1_weights"], inp["gemm1_weights_scale"], inp["gemm2_weights"],
                 inp["gemm2_weights_scale"], inp["routed_scaling_factor"])
 
-    def step(inp, use_timer):
-        if peer:   # the stage timer has no EP form: stages are timed separately below
+    def step(inp, use_timer=False):
+        """One timed step: the product call (moe_swarm_b200.run, or the peer-memory EP layer), then
+        the reduce-scatter when the combine is NCCL's."""
+        if peer:
             return layer.forward(*layer_args(inp), combine="peer", out=shard)
         out = timer.run(inp) if use_timer else M.run(**inp)
         if world > 1:
@@ -553,7 +635,7 @@ def main():
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record()
     for _ in range(steps):
-        step(x, True)
+        step(x)
     end.record()
     torch.cuda.synchronize()
     clocks.mark_end()
@@ -564,11 +646,38 @@ def main():
     status = M.device_status(device, T, E_GLOBAL // world)
     if status:
         raise RuntimeError(f"rank {rank}: device status {status:#x} after the timed steps (a bounded wait gave up)")
-    if peer:   # stage split of the same layer without the combine (untimed for the line's value)
-        for _ in range(steps):
-            timer.run(x)
-        torch.cuda.synchronize()
+    # stage split and the dominant kernel's launch time: the same layer calls with CUDA events
+    # between the stages on the launching stream, in their own loop (events between kernels break
+    # the programmatic-launch overlap, so these calls are not the timed ones)
+    timer.read(reset=True)
+    for _ in range(steps):
+        timer.run(x)
+    torch.cuda.synchronize()
     stage_ms, calls = timer.read(reset=True)
+
+    # the skewed-load variant of the workload (config 2's per-expert logit bias N(0, 0.5)): same
+    # weights, activations from the skewed generator, timed like the main steps
+    import moe_swarm_b200.workload as W
+    xs = dict(x)
+    xs.update({k: v.to(device) for k, v in W.make_activations(EP_T, 0, skew=0.5).items()})
+    fs = routing_facts(xs)
+    for _ in range(warmup):
+        step(xs)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    s3, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s3.record()
+    for _ in range(steps):
+        step(xs)
+    e3.record()
+    torch.cuda.synchronize()
+    ts = torch.tensor([s3.elapsed_time(e3)], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(ts, op=dist.ReduceOp.MAX)
+    skew_ms = float(ts[0]) / steps
+    del xs
     visible = None
     ck = clocks.stop(visible) if rank == 0 else None
     t = torch.tensor([ms] + stage_ms, device=device, dtype=torch.float64)
@@ -660,8 +769,9 @@ def main():
     cpu = None
     if world == 1 and rank == 0:
         if not args.no_sweeps:
-            sweeps, sweep_meta = sweep(device, steps, pk)
-        cpu = cpu_sample(act_cpu, world, k_experts=args.cpu_experts)
+            sweeps, sweep_meta = sweep(device, steps, pk, cpu=not args.no_cpu)
+        if not args.no_cpu:
+            cpu = cpu_baseline_ep(act_cpu, slice_weights_cpu(x), steps=1)
 
     if world > 1:
         import torch.distributed as dist
@@ -712,6 +822,10 @@ def main():
                         "the neighbouring steps' layers",
                 "serial_value": round(T / (e2e_serial_ms * 1e-3), 1),
                 "serial_ms_per_step": round(e2e_serial_ms, 4)},
+        "skewed_variant": {"value": round(T / (skew_ms * 1e-3), 1), "unit": "tokens/s",
+                           "ms_per_step": round(skew_ms, 4), "logit_skew": 0.5,
+                           "routing": {"active_experts_rank0": fs["active"], "rows_rank0": fs["rows"],
+                                       "max_rows_per_expert_rank0": int(fs["e_count"].max())}},
         "gpu_launches": launches_per_step * steps,
         "clocks": ck,
     }
