@@ -666,9 +666,11 @@ __global__ void __launch_bounds__(kFinThreads) stream_fin1_kernel(TileArgs g, in
 }
 
 // Launched as a programmatic dependent of GEMM1.
+// Four CTAs per GEMM CTA: a warp finishes its (tile, column) pairs one after another, each a chain
+// of dependent loads, so more warps than pairs keep that chain to one round.
 cudaError_t stream_fin_launch(int G, cudaStream_t st, const TileArgs& g) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(G);
+  cfg.gridDim = dim3(4 * G);
   cfg.blockDim = dim3(kFinThreads);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
