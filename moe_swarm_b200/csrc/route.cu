@@ -118,7 +118,18 @@ __device__ void prefetch_tokens(const RouteArgs& a, int t0, int nt, int tid, int
 // Routes token t with the calling warp: writes its top-8 (ascending expert id) with weights,
 // its local picks (ascending local expert) and their count, and adds the local picks to the
 // token's chunk histogram.
+// Phase times of the first routed token (traced builds): slots 6.. of CTA 0's routing record.
+#ifdef MOE_TRACE
+#define MOE_RT_MARK(i)                                                                         \
+  do {                                                                                         \
+    if (a.trace && blockIdx.x == 0 && threadIdx.x == 0) a.trace[6 + (i)] = globaltimer_ns(); \
+  } while (0)
+#else
+#define MOE_RT_MARK(i) (void)0
+#endif
+
 __device__ void route_token(const RouteArgs& a, const PickBuf& pb, const float* s_bias, int t, int lane) {
+  MOE_RT_MARK(0);
   const float* lg = a.logits + static_cast<size_t>(t) * kEG + lane * 8;
   const float4 v0 = *reinterpret_cast<const float4*>(lg);
   const float4 v1 = *reinterpret_cast<const float4*>(lg + 4);
@@ -129,9 +140,10 @@ __device__ void route_token(const RouteArgs& a, const PickBuf& pb, const float* 
     // sigmoid as 1/(1+exp(-x)) in fp32 (reference_official.py:99) with exp(-x) rounded
     // once to fp32 from a double evaluation (the correctly rounded fp32 exponential).
     const float e = exp_to_f32(-static_cast<double>(x[i]));
-    s[i] = 1.0f / (1.0f + e);
+    s[i] = __frcp_rn(1.0f + e);   // correctly rounded 1 / (1 + e): the IEEE quotient, bit for bit
     sb[i] = s[i] + s_bias[lane * 8 + i];
   }
+  MOE_RT_MARK(1);
   // group score: sum of the group's top-2 selection scores (multiset top-2)
   float m1 = -INFINITY, m2 = -INFINITY;
 #pragma unroll
@@ -162,34 +174,40 @@ __device__ void route_token(const RouteArgs& a, const PickBuf& pb, const float* 
     rank += (o > gscore || (o == gscore && h < g)) ? 1 : 0;
   }
   const bool keep = rank < kTopKGroup;
-  // top-8 among the kept groups: 8 rounds of a warp-wide argmax (ties -> lower expert id).
-  // Each lane keeps the key of its best remaining expert; a round is one warp max (redux) and
-  // a ballot for the lowest lane holding it, and only the winning lane rescans its slots.
-  uint32_t taken = 0;
-  auto lane_best = [&](uint32_t& key, int& slot) {
-    key = 0;
-    slot = 0;
+  MOE_RT_MARK(2);
+  // top-8 among the kept groups: 8 rounds of a warp-wide argmax (ties -> lower expert id).  Each
+  // lane first sorts its 8 candidates descending by (key, lower slot first) with a 19-comparator
+  // network on distinct composite keys; a round is then one warp max (redux), a ballot for the
+  // lowest lane holding it, and a shift of the winning lane's list -- no rescan on the chain.
+  uint64_t cand[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const uint32_t k = keep && !((taken >> i) & 1u) ? orderable(sb[i]) : 0u;
-      if (k > key) {
-        key = k;
-        slot = i;
-      }
-    }
+  for (int i = 0; i < 8; ++i)
+    cand[i] = (static_cast<uint64_t>(keep ? orderable(sb[i]) : 0u) << 3) | static_cast<uint64_t>(7 - i);
+  auto cx = [&](int x, int y) {   // descending
+    const uint64_t a = cand[x], b = cand[y];
+    cand[x] = a > b ? a : b;
+    cand[y] = a > b ? b : a;
   };
-  uint32_t bkey;
-  int bslot;
-  lane_best(bkey, bslot);
-#pragma unroll 1
+  cx(0, 2); cx(1, 3); cx(4, 6); cx(5, 7);
+  cx(0, 4); cx(1, 5); cx(2, 6); cx(3, 7);
+  cx(0, 1); cx(2, 3); cx(4, 5); cx(6, 7);
+  cx(2, 4); cx(3, 5);
+  cx(1, 4); cx(3, 6);
+  cx(1, 2); cx(3, 4); cx(5, 6);
+  uint32_t taken = 0;
+#pragma unroll
   for (int r = 0; r < kTopK; ++r) {
+    const uint32_t bkey = static_cast<uint32_t>(cand[0] >> 3);
     const uint32_t m = __reduce_max_sync(0xffffffffu, bkey);
     const uint32_t holders = __ballot_sync(0xffffffffu, bkey == m);
     if (lane == __ffs(holders) - 1) {
-      taken |= 1u << bslot;
-      lane_best(bkey, bslot);
+      taken |= 1u << (7 - static_cast<int>(cand[0] & 7u));
+#pragma unroll
+      for (int i = 0; i < 7; ++i) cand[i] = cand[i + 1];
+      cand[7] = 0;
     }
   }
+  MOE_RT_MARK(3);
   // combine weights from s (no bias): s / (sum + 1e-20) * rsf (reference_official.py:122-126)
   float part = 0.f;
 #pragma unroll
@@ -237,6 +255,7 @@ __device__ void route_token(const RouteArgs& a, const PickBuf& pb, const float* 
     a.tok_nloc[t] = nloc;
     pb.nloc[t] = nloc;
   }
+  MOE_RT_MARK(4);
 }
 
 // Pre-routed token t (moe_b200_forward_routed): the caller's 8 picks (global expert id and

@@ -509,23 +509,12 @@ __global__ void __launch_bounds__(kSThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   StreamSmem<MODE>& sm =
       *reinterpret_cast<StreamSmem<MODE>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  // GEMM1 depends on the routing kernel for everything; GEMM2 reads only the plan (routing,
-  // complete once GEMM1 started) before its own wait, so it can prefetch weights while
-  // GEMM1 finishes.
-  if (MODE == 1) {
-    pdl_wait();
-    pdl_launch_dependents();
-  }
-  const Plan plan = *g.plan;
-  Sched sk;
-  sk.init(plan.tt * SCfg<MODE>::NT, gridDim.x, SCfg<MODE>::KB);
-  if (plan.tt == 0 || !sk.has_work(blockIdx.x)) return;   // no work for this CTA
+  // The barriers, the tensor-map prefetches and the TMEM allocation depend on no earlier kernel:
+  // they run before the dependency wait.  GEMM1 depends on the routing kernel for everything
+  // else; GEMM2 reads only the plan (routing, complete once GEMM1 started) before its own wait,
+  // so it can prefetch weights while GEMM1 and the finalize end.  Both let their dependent
+  // kernel launch at once, so its CTAs are resident and waiting when this grid ends.
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int i = threadIdx.x; i <= g.E; i += blockDim.x) {
-    sm.e_cnt[i] = i < g.E ? g.e_count[i] : 0;
-    sm.e_start[i] = g.e_start[i];
-    sm.e_tt[i] = g.e_tiles[i];
-  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < SCfg<MODE>::STAGES; ++s) {
       mbar_init(&sm.full[s], 1);
@@ -546,9 +535,25 @@ __global__ void __launch_bounds__(kSThreads, 1)
     tmem_alloc(&sm.tmem_base, 512);
     tmem_relinquish();
   }
+  if (MODE == 1) pdl_wait();
+  pdl_launch_dependents();
+  const Plan plan = *g.plan;
+  Sched sk;
+  sk.init(plan.tt * SCfg<MODE>::NT, gridDim.x, SCfg<MODE>::KB);
+  const bool work = plan.tt != 0 && sk.has_work(blockIdx.x);
+  if (work)
+    for (int i = threadIdx.x; i <= g.E; i += blockDim.x) {
+      sm.e_cnt[i] = i < g.E ? g.e_count[i] : 0;
+      sm.e_start[i] = g.e_start[i];
+      sm.e_tt[i] = g.e_tiles[i];
+    }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  if (!work) {   // no work for this CTA
+    if (warp == 1) tmem_dealloc(sm.tmem_base, 512);
+    return;
+  }
 #ifdef MOE_TRACE
   if (threadIdx.x == 0) g.trace[blockIdx.x * kTraceSlots + 0] = globaltimer_ns();
 #endif
@@ -578,6 +583,22 @@ cudaError_t stream_prepare() {
                               static_cast<int>(stream_smem_bytes<2>()));
 }
 
+// The plan read through L2 only (it may have been written by another grid after this SM cached it).
+__device__ __forceinline__ Plan ld_cg_plan(const Plan* p) {
+  const int4* q = reinterpret_cast<const int4*>(p);
+  const int4 a = __ldcg(q), b = __ldcg(q + 1);
+  Plan r;
+  r.T = a.x;
+  r.E = a.y;
+  r.rows = a.z;
+  r.m_tiles = a.w;
+  r.tt = b.x;
+  r.pad[0] = b.y;
+  r.pad[1] = b.z;
+  r.pad[2] = b.w;
+  return r;
+}
+
 // Shared memory of stream_fin1_kernel: the tile tables.
 struct FinSmem {
   int e_cnt[kEG + 1];
@@ -598,16 +619,18 @@ constexpr int kFinThreads = 256;
 __global__ void __launch_bounds__(kFinThreads) stream_fin1_kernel(TileArgs g, int G) {
   __shared__ FinSmem sm;
   MOE_TRACE_CTA(g.trace, 0);
+  pdl_launch_dependents();    // GEMM2 may start its prologue and weight prefetch
+  // The plan and the tile tables come from the routing, which completed before GEMM1 passed its
+  // own dependency wait (and so before this grid was launched): they are read before this grid's
+  // wait, from L2, while GEMM1 still runs.
+  const Plan plan = ld_cg_plan(g.plan);
+  for (int i = threadIdx.x; i <= g.E; i += blockDim.x) {
+    sm.e_cnt[i] = i < g.E ? __ldcg(g.e_count + i) : 0;
+    sm.e_start[i] = __ldcg(g.e_start + i);
+    sm.e_tt[i] = __ldcg(g.e_tiles + i);
+  }
   pdl_wait();                 // the partials come from GEMM1
   MOE_TRACE_CTA(g.trace, 2);
-  pdl_launch_dependents();    // GEMM2 may start its prologue and weight prefetch
-  const Plan plan = *g.plan;
-  // the tables do not depend on the plan: their loads go out together with the plan's
-  for (int i = threadIdx.x; i <= g.E; i += blockDim.x) {
-    sm.e_cnt[i] = i < g.E ? g.e_count[i] : 0;
-    sm.e_start[i] = g.e_start[i];
-    sm.e_tt[i] = g.e_tiles[i];
-  }
   Sched sk;
   sk.init(plan.tt * SCfg<1>::NT, G, SCfg<1>::KB);
   const int nsplit = sk.tiles - sk.dp;   // stream-K tiles

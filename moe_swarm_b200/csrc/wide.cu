@@ -578,10 +578,10 @@ __global__ void __launch_bounds__(kWThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   WideSmem<MODE>& sm =
       *reinterpret_cast<WideSmem<MODE>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  if (MODE == 1) {
-    pdl_wait();
-    pdl_launch_dependents();
-  }
+  // GEMM1 waits for the routing; GEMM2 reads only the plan before its epilogue's wait.  Both let
+  // their dependent kernel (GEMM2, the combine) launch at once.
+  if (MODE == 1) pdl_wait();
+  pdl_launch_dependents();
   const Plan plan = *g.plan;
   const int ntiles = plan.m_tiles * WCfg<MODE>::NT;
   Sched sk;
