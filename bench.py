@@ -686,16 +686,19 @@ def main():
     ms, stage_ms = float(t[0]), [float(v) for v in t[1:]]
     ms_per_step = ms / steps
 
-    # e2e: host (pinned) activations -> device, layer, reduce-scatter, result -> host.
+    # e2e: host (pinned) activations -> device, layer, combine, result -> host.
     # Serial: each step's copies and layer back to back on one stream.  Pipelined (the
     # reported value): two buffer sets; step i+1's inputs upload on a copy stream while step i's
     # layer runs, and step i's result downloads on another while step i+1 runs -- every step's
     # bytes still cross PCIe inside the timed region, which runs from the first upload to the
-    # last download.
+    # last download.  With N > 1 ranks each rank uploads only its T/N tokens' activations and an
+    # NCCL all-gather over NVLink assembles the replicated inputs on every rank (the broadcast
+    # form of expert parallelism needs every token on every rank; 1/N of it crosses each host
+    # link), in stream order before the layer.
     names = ("routing_logits", "routing_bias", "hidden_states", "hidden_states_scale")
-    host = {k: act_cpu[k].contiguous().pin_memory() for k in names}
+    n_tok = T // world
+    lo_t = rank * n_tok
     out_shape = tuple(shard.shape) if world > 1 else (T, H)
-    h2d = sum(v.numel() * v.element_size() for v in host.values())
     d2h = out_shape[0] * out_shape[1] * 2
     NB = 2
     dev_in = [{k: torch.empty_like(x[k]) for k in names} for _ in range(NB)]
@@ -706,6 +709,32 @@ def main():
     s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
     ev = {n: [torch.cuda.Event() for _ in range(NB)] for n in ("in_ready", "in_free", "out_ready", "out_free")}
     used = [False] * NB
+    gat_scale = [torch.empty((world, 56, n_tok), dtype=torch.float32, device=device) for _ in range(NB)]
+
+    def input_plan(sharded):
+        """Host tensors each rank uploads per step and the device buffers they land in: every
+        rank's whole inputs ("full"), or (N > 1, "sharded") its own T/N tokens, replicated by an
+        NCCL all-gather over NVLink in stream order before the layer."""
+        if sharded:
+            host = {"routing_logits": act_cpu["routing_logits"][lo_t:lo_t + n_tok],
+                    "routing_bias": act_cpu["routing_bias"],
+                    "hidden_states": act_cpu["hidden_states"][lo_t:lo_t + n_tok].view(torch.uint8),
+                    "hidden_states_scale": act_cpu["hidden_states_scale"][:, lo_t:lo_t + n_tok]}
+        else:
+            host = {k: act_cpu[k] for k in names}
+        host = {k: v.contiguous().pin_memory() for k, v in host.items()}
+        up = [{k: torch.empty_like(v, device=device) for k, v in host.items()} for _ in range(NB)] if sharded else dev_in
+        return host, up
+
+    def assemble(b, up, sharded):
+        if not sharded:
+            return
+        d, u = dev_in[b], up[b]
+        dist.all_gather_into_tensor(d["routing_logits"], u["routing_logits"])
+        dist.all_gather_into_tensor(d["hidden_states"].view(torch.uint8), u["hidden_states"])
+        dist.all_gather_into_tensor(gat_scale[b], u["hidden_states_scale"])
+        d["hidden_states_scale"].view(56, world, n_tok).copy_(gat_scale[b].permute(1, 0, 2))
+        d["routing_bias"].copy_(u["routing_bias"])
 
     def layer_into(inp, dst):
         if peer:
@@ -715,23 +744,25 @@ def main():
         else:
             M.run(**inp, out=dst)
 
-    def e2e_serial_step():
-        for k in names:
-            dev_in[0][k].copy_(host[k], non_blocking=True)
+    def e2e_serial_step(host, up, sharded):
+        for k in host:
+            up[0][k].copy_(host[k], non_blocking=True)
+        assemble(0, up, sharded)
         layer_into(xe[0], dev_out[0])
         res_host[0].copy_(dev_out[0], non_blocking=True)
 
-    def e2e_pipelined_step(i):
+    def e2e_pipelined_step(i, host, up, sharded):
         b = i % NB
         with torch.cuda.stream(s_in):
             if used[b]:
                 s_in.wait_event(ev["in_free"][b])     # step i-2's layer has read these inputs
-            for k in names:
-                dev_in[b][k].copy_(host[k], non_blocking=True)
+            for k in host:
+                up[b][k].copy_(host[k], non_blocking=True)
             ev["in_ready"][b].record(s_in)
         cs.wait_event(ev["in_ready"][b])
         if used[b]:
             cs.wait_event(ev["out_free"][b])          # step i-2's result has left for the host
+        assemble(b, up, sharded)
         layer_into(xe[b], dev_out[b])
         ev["in_free"][b].record(cs)
         ev["out_ready"][b].record(cs)
@@ -757,13 +788,23 @@ def main():
             dist.all_reduce(te, op=dist.ReduceOp.MAX)
         return float(te[0]) / steps
 
+    host_full, up_full = input_plan(False)
     for _ in range(2):
-        e2e_serial_step()
-    e2e_serial_ms = timed(lambda: [e2e_serial_step() for _ in range(steps)], cs)
-    for i in range(2):
-        e2e_pipelined_step(i)
-    e2e_ms = timed(lambda: [e2e_pipelined_step(i) for i in range(steps)], s_in)
-    assert torch.equal(res_host[(steps - 1) % NB].view(torch.int16), dev_out[(steps - 1) % NB].cpu().view(torch.int16))
+        e2e_serial_step(host_full, up_full, False)
+    e2e_serial_ms = timed(lambda: [e2e_serial_step(host_full, up_full, False) for _ in range(steps)], cs)
+    e2e_modes = {}
+    for sharded in ((False, True) if world > 1 else (False,)):
+        host, up = input_plan(sharded)
+        used[:] = [False] * NB
+        for i in range(2):
+            e2e_pipelined_step(i, host, up, sharded)
+        e2e_modes["sharded" if sharded else "full"] = (
+            timed(lambda: [e2e_pipelined_step(i, host, up, sharded) for i in range(steps)], s_in),
+            sum(v.numel() * v.element_size() for v in host.values()))
+        assert torch.equal(res_host[(steps - 1) % NB].view(torch.int16),
+                           dev_out[(steps - 1) % NB].cpu().view(torch.int16))
+    e2e_mode = min(e2e_modes, key=lambda m: e2e_modes[m][0])
+    e2e_ms, h2d = e2e_modes[e2e_mode]
 
     sweeps = None
     cpu = None
@@ -818,8 +859,12 @@ def main():
                      "peak_source": pk["source"] + " (MEASURED_PEAKS.json hbm_gbs, burst copy)"},
         "e2e": {"value": round(T / (e2e_ms * 1e-3), 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4),
-                "mode": "pipelined: 2 buffer sets, uploads and downloads on their own streams overlap "
-                        "the neighbouring steps' layers",
+                "mode": ("pipelined: 2 buffer sets, uploads and downloads on their own streams overlap "
+                         "the neighbouring steps' layers; inputs: "
+                         + ("each rank uploads its T/N tokens, an NCCL all-gather over NVLink replicates them"
+                            if e2e_mode == "sharded" else "every rank uploads the whole step's inputs")),
+                "by_input_mode": {m: {"value": round(T / (v[0] * 1e-3), 1), "h2d_bytes_per_step": v[1]}
+                                  for m, v in e2e_modes.items()},
                 "serial_value": round(T / (e2e_serial_ms * 1e-3), 1),
                 "serial_ms_per_step": round(e2e_serial_ms, 4)},
         "skewed_variant": {"value": round(T / (skew_ms * 1e-3), 1), "unit": "tokens/s",
