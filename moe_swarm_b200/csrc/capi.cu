@@ -167,10 +167,18 @@ int prepare(const moe_b200_args* a, void* workspace, size_t ws_bytes, moe::Layou
 // zero_rows: the routing kernels also write the zero output rows of tokens with no local
 // expert (moe_b200_route); the full layer leaves them to the combine kernel instead, which
 // runs on every SM rather than on the single routing CTA of small batches.
+// copy_rows: the permutation also copies the activation rows and their scales into the
+// workspace (the token-major GEMMs read them from there); the streaming GEMM1 gathers its token
+// rows from hidden_states itself, so the streaming path passes false.
 int launch_route(const moe_b200_args* a, uint8_t* ws, const moe::Layout& L, int sms, cudaStream_t st,
-                 int* launches, bool zero_rows, const int32_t* pre_idx = nullptr, const float* pre_w = nullptr) {
+                 int* launches, bool zero_rows, const int32_t* pre_idx = nullptr, const float* pre_w = nullptr,
+                 bool copy_rows = true) {
   moe::RouteArgs r = make_route_args(a, ws, L, sms);
   if (!zero_rows) r.out = nullptr;
+  if (!copy_rows) {
+    r.a_perm = nullptr;
+    r.sa_perm = nullptr;
+  }
   r.pre_idx = pre_idx;
   r.pre_w = pre_w;
   cudaError_t e = moe::route_launch(r, st, launches);
@@ -270,6 +278,7 @@ moe::TileArgs tile_args(const moe_b200_args* a, uint8_t* ws, const moe::Layout& 
   s.e_start = reinterpret_cast<const int*>(ws + L.e_start);
   s.E = a->num_local_experts;
   s.r_pad = L.r_pad;
+  s.sa_ld = L.r_pad;
   s.c_hi = ws + L.c_hi;
   s.c_lo = ws + L.c_lo;
   s.c_scale = reinterpret_cast<float*>(ws + L.c_scale);
@@ -326,14 +335,15 @@ int forward_impl(const moe_b200_args* a, void* workspace, size_t ws_bytes, void*
     cudaEventRecord(ev[0], st);
   }
   int launches = 0;
-  rc = launch_route(a, ws, L, di.sms, st, &launches, false, pre_idx, pre_w);
+  rc = launch_route(a, ws, L, di.sms, st, &launches, false, pre_idx, pre_w, a->num_tokens > moe::kStreamMaxT);
   if (rc) return rc;
   if (ev) cudaEventRecord(ev[1], st);
 
   const int E = a->num_local_experts;
   if (a->num_tokens <= moe::kStreamMaxT) {
     CUtensorMap mTok, mW13s, mHi, mLo, mW2s;
-    if (!encode_u8_2d(&mTok, ws + L.a_perm, moe::kH, L.r_pad, moe::kTok) ||
+    // token rows gathered four at a time from hidden_states (one-row boxes, tile::gather4)
+    if (!encode_u8_2d(&mTok, a->hidden_states, moe::kH, static_cast<uint64_t>(a->num_tokens), 1) ||
         !encode_u8_2d(&mW13s, a->gemm1_weights, moe::kH, (uint64_t)E * moe::kN1) ||
         !encode_u8_2d(&mHi, ws + L.c_hi, moe::kI, L.r_pad, moe::kTok) ||
         !encode_u8_2d(&mLo, ws + L.c_lo, moe::kI, L.r_pad, moe::kTok) ||
@@ -344,7 +354,9 @@ int forward_impl(const moe_b200_args* a, void* workspace, size_t ws_bytes, void*
     unsigned long long* trace = reinterpret_cast<unsigned long long*>(ws + L.trace);
     const int grid = di.sms < moe::kMaxSms ? di.sms : moe::kMaxSms;
     moe::TileArgs s1 = s;
-    s1.sa = reinterpret_cast<const float*>(ws + L.sa_perm);
+    s1.sa = a->hidden_states_scale;   // [56][T], read at each row's token
+    s1.sa_ld = static_cast<size_t>(a->num_tokens);
+    s1.sa_by_token = 1;
     s1.sw = a->gemm1_weights_scale;
     s1.trace = trace;
     cudaError_t e = moe::stream_launch(1, grid, st, mW13s, mTok, mTok, s1);

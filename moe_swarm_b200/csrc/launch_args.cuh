@@ -94,7 +94,9 @@ struct TileArgs {
   const int* e_tiles;   // per-expert prefix of this kernel's token tiles (E + 1 entries)
   int E;
   size_t r_pad;
-  const float* sa;   // MODE 1: activation scales [56][r_pad]; MODE 2: C scales [16][r_pad]
+  const float* sa;   // MODE 1: activation scales [56][sa_ld]; MODE 2: C scales [16][r_pad]
+  size_t sa_ld;      // leading dimension of sa
+  int sa_by_token;   // MODE 1 streaming: sa is hidden_states_scale [56][T], column = the row's token
   const float* sw;   // MODE 1: gemm1_weights_scale [E][32][56]; MODE 2: gemm2_weights_scale [E][56][16]
   uint8_t* c_hi;
   uint8_t* c_lo;

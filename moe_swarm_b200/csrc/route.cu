@@ -96,16 +96,16 @@ __device__ __forceinline__ PickBuf global_picks(const RouteArgs& a) {
   return PickBuf{a.tok_le, a.tok_lw, a.tok_nloc, a.chunk_hist};
 }
 
-// Starts tokens [t0, t0 + nt) on their way to L2: their logits rows and, when the activation
-// rows are copied, their hidden rows and 56 scales -- so those loads find L2 rather than HBM
-// once the routing, which needs none of them but the logits, is done.
+// Starts tokens [t0, t0 + nt) on their way to L2: their logits rows and, in the layer call,
+// their hidden rows and 56 scales -- so the scatter's copies (and the streaming GEMM1's row
+// gathers) find them in L2 rather than HBM once the routing, which needs only the logits, is done.
 __device__ void prefetch_tokens(const RouteArgs& a, int t0, int nt, int tid, int nthr) {
   if (nt <= 0) return;
   if (a.logits) {
     const char* lg = reinterpret_cast<const char*>(a.logits + static_cast<size_t>(t0) * kEG);
     for (int i = tid; i < nt * (kEG * 4 / 128); i += nthr) prefetch_l2(lg + static_cast<size_t>(i) * 128);
   }
-  if (!a.a_perm || !a.hidden) return;
+  if (!a.hidden) return;   // (rows are copied by the scatter, or gathered by the streaming GEMM1)
   const uint8_t* h = a.hidden + static_cast<size_t>(t0) * kH;
   for (int i = tid; i < nt * (kH / 128); i += nthr) prefetch_l2(h + static_cast<size_t>(i) * 128);
   // scales [56][T]: the run of nt floats of each K-block, its first and last line

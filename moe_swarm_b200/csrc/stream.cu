@@ -150,6 +150,16 @@ __device__ void s_producer(StreamSmem<MODE>& sm, const CUtensorMap* tmW, const C
   int tile, k0, k1;
   while (it.next(tile, k0, k1)) {
     const STile s = s_decode<MODE>(sm, g.E, tile);
+    // MODE 1: lanes 2..9 gather the tile's 32 token rows from hidden_states, four per lane (rows
+    // past the tile's tokens repeat its last token; their products are never stored)
+    int tk0 = 0, tk1 = 0, tk2 = 0, tk3 = 0;
+    if (MODE == 1 && lane >= 2 && lane < 2 + kTok / 4) {
+      const int j = 4 * (lane - 2), last = s.row0 + s.nr - 1;
+      tk0 = __ldg(g.row_token + min(s.row0 + j, last));
+      tk1 = __ldg(g.row_token + min(s.row0 + j + 1, last));
+      tk2 = __ldg(g.row_token + min(s.row0 + j + 2, last));
+      tk3 = __ldg(g.row_token + min(s.row0 + j + 3, last));
+    }
     for (int kb = k0; kb < k1; ++kb) {
       const long long t0 = MOE_TCLK();
       const bool ok = mbar_wait(&sm.empty[stage], phase ^ 1u, &sm.abort, g.status, kStWaitProducer);
@@ -162,7 +172,8 @@ __device__ void s_producer(StreamSmem<MODE>& sm, const CUtensorMap* tmW, const C
       if (MODE == 1) {
         if (lane == 0) tma_load_2d(st, tmW, &sm.full[stage], kb * kBlk, s.e * kN1 + s.nt * kBlk);
         if (lane == 1) tma_load_2d(st + 16384, tmW, &sm.full[stage], kb * kBlk, s.e * kN1 + kI + s.nt * kBlk);
-        if (lane == 2) tma_load_2d(st + 32768, tmT, &sm.full[stage], kb * kBlk, s.row0);
+        if (lane >= 2 && lane < 2 + kTok / 4)
+          tma_gather4(st + 32768 + 512 * (lane - 2), tmT, &sm.full[stage], kb * kBlk, tk0, tk1, tk2, tk3);
       } else {
         if (lane == 2) tma_load_2d(st, tmW, &sm.full[stage], kb * kBlk, s.e * kH + s.nt * kBlk);
         if (!waited) {
@@ -377,7 +388,8 @@ __device__ void s_epilogue(StreamSmem<MODE>& sm, uint32_t tmem, const TileArgs& 
     }
     // stage the segment's scales in shared memory: one round of independent loads per
     // segment instead of an L2 round trip on every K-block's critical path
-    for (int i = q; i < k1 - k0; i += 4) sm.ssa[i][lane] = __ldg(g.sa + static_cast<size_t>(k0 + i) * g.r_pad + srow);
+    const size_t scol = MODE == 1 && g.sa_by_token ? static_cast<size_t>(__ldg(g.row_token + srow)) : srow;
+    for (int i = q; i < k1 - k0; i += 4) sm.ssa[i][lane] = __ldg(g.sa + static_cast<size_t>(k0 + i) * g.sa_ld + scol);
     if (q == 0)
       for (int i = lane; i < k1 - k0; i += 32) {
         sm.ssw[0][i] = __ldg(swp1 + k0 + i);
