@@ -1,6 +1,7 @@
 // DeepSeek-V3 no-aux routing fused with the token->expert histogram, the prefix sums
-// (expert segments and GEMM tile tables) and the permutation of activation rows into
-// expert-major order.
+// (expert segments and GEMM tile tables) and the permutation into expert-major order: the row
+// metadata always, and for the token-major GEMMs (T > 512) the activation rows and their scales
+// copied into the workspace (the streaming GEMM1 gathers its rows from hidden_states itself).
 //
 // Semantics follow spec/reference_official.py:95-126 (selection on sigmoid(logits)+bias,
 // 8 groups scored by their top-2 sum, 4 groups kept, top-8 experts, bias-free weights
@@ -19,7 +20,7 @@
 // a popcount over the chunk's per-expert token bitmask plus the chunk base.  At decode sizes
 // one CTA does all of it in one launch with the pick lists and counts in shared memory.  Each
 // routing CTA first starts its tokens' hidden rows and scales toward L2, so the permutation's
-// copies find them there.
+// copies (or GEMM1's gathers) find them there.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 

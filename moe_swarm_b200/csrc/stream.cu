@@ -8,6 +8,8 @@
 //     and 128 X2 rows [2048+128nt, +128)); K = 56 blocks of 128.
 //       D1 = W13[X1 rows] . A^T,  D2 = W13[X2 rows] . A^T   (fp8 x fp8 -> fp32 TMEM)
 //       acc_i[r][c] += D_i[r][c] * s13[e, block_i, kb] * sa[token c, kb]   (exact fp32 scales)
+//     The token tile A is gathered straight from hidden_states, four rows per TMA tile::gather4
+//     (the routing writes only the permutation, no row copies), and sa is read at each token.
 //     epilogue: C = silu(X2) * X1 per (feature r, token c); per-token amax over the tile's
 //     128 features; C stored as the e4m3 pair C ~= s*(hi + lo), hi = e4m3(C/s),
 //     lo = e4m3(C/s - hi), s = amax/448.  A tile that stream-K split over several CTAs is
