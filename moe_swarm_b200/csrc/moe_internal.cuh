@@ -28,8 +28,10 @@ constexpr int kTok = 32;          // token tile (MMA N) of the streaming kernels
 constexpr int kMaxSms = 256;      // partial-slot capacity of the stream-K fixup (2 per CTA)
 constexpr int kStreamMaxT = 512;  // T above which the wide (token-major) kernels run
 constexpr int kTraceSlots = 16;   // per-CTA counters of a traced build (MOE_TRACE)
-constexpr int kTraceKernels = 8;  // stream GEMM1, stream GEMM2, wide GEMM1, wide GEMM2, routing,
-                                  // scatter, GEMM1 finalize, combine
+constexpr int kTraceKernels = 10; // stream GEMM1, stream GEMM2, wide GEMM1, wide GEMM2, routing,
+                                  // scatter, GEMM1 finalize, combine; then the per-K-block handoff
+                                  // timelines of CTA 0 of wide GEMM1 and wide GEMM2
+constexpr int kTimelineKBs = 256; // K-blocks recorded per timeline (rows of kTimelineKBs stamps)
 
 // Bound of every device-side wait (mbarrier phases, stream-K arrivals, peer flags): far above
 // any legitimate stall.  The peer-flag wait of expert parallelism takes a caller-given bound

@@ -38,9 +38,19 @@ namespace moe {
 #ifdef MOE_TRACE
 #define MOE_WCLK() clock64()
 #define MOE_WADD(var, t0) (var) += clock64() - (t0)
+// Per-K-block handoff timeline of CTA 0 (traced builds): `clock64` stamps in the trace region six
+// kernel blocks past this kernel's counters (trace kernels 8 and 9), row-major [row][K-block]:
+// row 0 MMA thread has a free accumulator, 1 its operand stage is full, 2 its MMAs and commits are
+// issued, 3 the first promotion warp sees the accumulator, 4 + w promotion warp w releases it.
+#define MOE_TL(g, row, n)                                                                          \
+  do {                                                                                             \
+    if (blockIdx.x == 0 && (n) < kTimelineKBs)                                                     \
+      (g).trace[6 * kMaxSms * kTraceSlots + (row) * kTimelineKBs + (n)] = clock64();               \
+  } while (0)
 #else
 #define MOE_WCLK() 0ll
 #define MOE_WADD(var, t0) (void)0
+#define MOE_TL(g, row, n) (void)0
 #endif
 
 template <int MODE>
@@ -207,6 +217,7 @@ __device__ __forceinline__ void w_mma(WideSmem<MODE>& sm, uint32_t tmem, const T
   constexpr int ST = WCfg<MODE>::STAGES;
   constexpr uint32_t idesc = idesc_e4m3_f32(128, 256);
   uint32_t stage = 0, phase = 0, tk = 0, buf = 0;
+  int nkb = 0;
   long long tw_t = 0, tw_f = 0, t_first = 0, t_iss = 0;
   SegIter it(sk, blockIdx.x);
   int tile, k0, k1;
@@ -215,9 +226,11 @@ __device__ __forceinline__ void w_mma(WideSmem<MODE>& sm, uint32_t tmem, const T
       long long t0 = MOE_WCLK();
       if (!mbar_wait(&sm.tempty[buf], ((tk >> buf) & 1u) ^ 1u, &sm.abort, g.status, kStWaitMmaTmem))
         goto done;
+      MOE_TL(g, 0, nkb);
       MOE_WADD(tw_t, t0);
       t0 = MOE_WCLK();
       if (!mbar_wait(&sm.full[stage], phase, &sm.abort, g.status, kStWaitMma)) goto done;
+      MOE_TL(g, 1, nkb);
       MOE_WADD(tw_f, t0);
 #ifdef MOE_TRACE
       if (t_first == 0) t_first = static_cast<long long>(globaltimer_ns());
@@ -241,6 +254,8 @@ __device__ __forceinline__ void w_mma(WideSmem<MODE>& sm, uint32_t tmem, const T
       }
       mma_commit(&sm.empty[stage]);
       mma_commit(&sm.tfull[buf]);
+      MOE_TL(g, 2, nkb);
+      ++nkb;
       MOE_WADD(t_iss, t0);
       tk ^= 1u << buf;
       buf ^= 1u;
@@ -368,6 +383,7 @@ __device__ __forceinline__ void w_epilogue(WideSmem<MODE>& sm, uint32_t tmem, co
   const int rit = q * 32 + lane;
   const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
   uint32_t tk = 0, buf = 0;
+  int nkb = 0;
   bool dead = false;
   long long tw = 0, tp = 0, te = 0, tf = 0, ts = 0;
   if (MODE == 2) pdl_wait();   // the C scales and the combine inputs come from GEMM1
@@ -432,12 +448,14 @@ __device__ __forceinline__ void w_epilogue(WideSmem<MODE>& sm, uint32_t tmem, co
       t0 = MOE_WCLK();
       if (!dead && !mbar_wait(&sm.tfull[buf], (tk >> buf) & 1u, &sm.abort, g.status, kStWaitEpilogue))
         dead = true;
+      if (warp == 4 && lane == 0) MOE_TL(g, 3, nkb);
       MOE_WADD(tw, t0);
       t0 = MOE_WCLK();
       if (!dead && !qlive) {
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.tempty[buf]);
+        if (lane == 0) MOE_TL(g, warp, nkb);   // row 4 + (warp - 4)
       }
       if (!dead && qlive) {
         // Promotion in four steps of 2 x 16 columns (MODE 1: X1 and X2 columns 64h + 16s ..;
@@ -467,6 +485,7 @@ __device__ __forceinline__ void w_epilogue(WideSmem<MODE>& sm, uint32_t tmem, co
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&sm.tempty[buf]);
+            if (lane == 0) MOE_TL(g, warp, nkb);   // row 4 + (warp - 4)
           }
           float* acc_a;
           float* acc_b;
@@ -492,6 +511,7 @@ __device__ __forceinline__ void w_epilogue(WideSmem<MODE>& sm, uint32_t tmem, co
         }
       }
       MOE_WADD(tp, t0);
+      ++nkb;
       if (MODE == 2 && ki == 0 && meta_mine) meta_k = __ldg(g.tok_nloc + meta_t);   // t arrived by now
       tk ^= 1u << buf;
       buf ^= 1u;

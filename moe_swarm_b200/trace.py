@@ -15,10 +15,17 @@ of the workspace cleared, and one JSON line per case gives, per kernel that ran:
   promotion wait and work, tile epilogue, stream-K fixup, scale staging; ``ns_per_kb`` (span per
   K-block) and, for the wide kernels, the SM clock the span ran at;
 * routing: the phase times of the first token (``rt_marks_us``: start, after the sigmoid, after
-  the group ranking, after the top-8, end) and the routing CTA's phase marks.
+  the group ranking, after the top-8, end) and the routing CTA's phase marks;
+* wide GEMMs (``wide_g1_timeline`` / ``wide_g2_timeline``): the accumulator handoff of CTA 0 per
+  K-block, medians over its K-blocks after the first 20 (cycles): the period, the MMA thread's
+  wait for a free accumulator and for its operand stage, its issue of the MMAs and commits, the
+  commit -> first promotion warp seeing the accumulator, the promotion until the last warp
+  releases it, and each promotion warp's release relative to the first promotion warp's
+  (``release_vs_w4``, median and 90th percentile, warps 4..11).
 
 Kernel order of the trace region: stream GEMM1, stream GEMM2, wide GEMM1, wide GEMM2, routing,
-scatter, GEMM1 finalize, combine (``moe_internal.cuh``, ``kTraceKernels``).
+scatter, GEMM1 finalize, combine, then the two wide-GEMM timelines (``moe_internal.cuh``,
+``kTraceKernels``).
 """
 
 from __future__ import annotations
@@ -34,6 +41,32 @@ from . import _workspace, device_status
 
 NAMES = ["stream_g1", "stream_g2", "wide_g1", "wide_g2", "route", "scatter", "fin1", "combine"]
 SLOTS, CTAS = 16, 256
+TL_BLOCKS, TL_KBS, TL_ROWS = 2, 256, 12   # wide GEMM1 / GEMM2 timelines: [row][K-block] stamps
+
+
+def timeline(tl: torch.Tensor) -> dict | None:
+    """Handoff medians of one wide-GEMM timeline ([TL_ROWS][TL_KBS] clock64 stamps, 0 = none)."""
+    n = int((tl[2] != 0).sum())
+    if n < 40:
+        return None
+    t = tl[:, 20:n].double()
+    t = t[:, (t != 0).all(dim=0)]
+    if t.shape[1] < 10:
+        return None
+    med = lambda x: round(x.median().item(), 1)
+    last_rel = t[4:12].max(dim=0).values
+    rel = t[4:12] - t[4]
+    return {
+        "kbs": int(t.shape[1]),
+        "period": med(t[2, 1:] - t[2, :-1]),
+        "mma_wait_acc": med(t[0, 1:] - t[2, :-1]),
+        "mma_wait_stage": med(t[1] - t[0]),
+        "mma_issue": med(t[2] - t[1]),
+        "commit_to_promotion": med(t[3] - t[2]),
+        "promotion_to_last_release": med(last_rel - t[3]),
+        "release_vs_w4": [med(rel[w]) for w in range(8)],
+        "release_vs_w4_p90": [round(rel[w].quantile(0.9).item(), 1) for w in range(8)],
+    }
 
 
 def run_case(T: int, E: int, skew: float = 0.0, seed: int = 5, calls: int = 4) -> dict:
@@ -44,7 +77,7 @@ def run_case(T: int, E: int, skew: float = 0.0, seed: int = 5, calls: int = 4) -
     x["routed_scaling_factor"] = 2.5
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     L = N.layout(T, E)
-    n = len(NAMES) * CTAS * SLOTS * 8
+    n = (len(NAMES) + TL_BLOCKS) * CTAS * SLOTS * 8
     for i in range(calls):
         flush.zero_()
         if i == calls - 1:
@@ -52,8 +85,14 @@ def run_case(T: int, E: int, skew: float = 0.0, seed: int = 5, calls: int = 4) -
             _workspace(dev).buf[L.trace:L.trace + n].zero_()
         run(**x)
     torch.cuda.synchronize()
-    tr = _workspace(dev).buf[L.trace:L.trace + n].view(torch.int64).view(len(NAMES), CTAS, SLOTS).cpu()
+    allt = _workspace(dev).buf[L.trace:L.trace + n].view(torch.int64).cpu()
+    tr = allt[:len(NAMES) * CTAS * SLOTS].view(len(NAMES), CTAS, SLOTS)
+    tls = allt[len(NAMES) * CTAS * SLOTS:].view(TL_BLOCKS, CTAS * SLOTS)[:, :TL_ROWS * TL_KBS]
     res = {"T": T, "E": E, "skew": skew, "status": device_status(dev)}
+    for b, nm in enumerate(("wide_g1_timeline", "wide_g2_timeline")):
+        d = timeline(tls[b].view(TL_ROWS, TL_KBS))
+        if d:
+            res[nm] = d
     live_any = [tr[k][tr[k][:, 0] != 0] for k in range(len(NAMES))]
     t0 = min(int(r[:, 0].min()) for r in live_any if len(r))
     for k, r in enumerate(live_any):
