@@ -89,9 +89,12 @@ struct StreamSmem {
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
-  int col_t[2][kTok];     // MODE 2 tile metadata, by segment parity: token,
-  int col_k[2][kTok];     // its local expert count
-  float col_w[2][kTok];   // and the row's combine weight
+  // MODE 2 tile metadata, by segment parity: where token column c's output row goes -- its bf16
+  // output row (bit 0 set) for a token with one local expert, else its fp32 partial row -- and
+  // the row's combine weight.  The destination is resolved once per segment and column, not at
+  // every store (the output map of expert parallelism divides and indexes per token).
+  uintptr_t col_dst[2][kTok];
+  float col_w[2][kTok];
   float colmax[4][kTok];
   float amax[kTok];
   int e_cnt[kEG + 1];
@@ -347,10 +350,11 @@ __device__ void s_epi2(StreamSmem<2>& sm, const TileArgs& g, const STile& s, con
   for (int c = 0; c < kTok; ++c) {
     if (c >= s.nr) break;
     const float v = __fmul_rn(acc[c], sm.col_w[par][c]);
-    if (sm.col_k[par][c] == 1)
-      out_row(g.out, sm.col_t[par][c])[f] = bf16_bits(v);
+    const uintptr_t d = sm.col_dst[par][c];
+    if (d & 1u)
+      reinterpret_cast<uint16_t*>(d & ~uintptr_t(1))[f] = bf16_bits(v);
     else
-      g.part2[static_cast<size_t>(s.row0 + c) * kH + f] = v;
+      reinterpret_cast<float*>(d)[f] = v;
   }
 }
 
@@ -401,9 +405,11 @@ __device__ void s_epilogue(StreamSmem<MODE>& sm, uint32_t tmem, const TileArgs& 
     // Double-buffered by segment parity: warps may still read the previous segment's copy.
     if (MODE == 2 && q == 1) {
       const bool live = lane < s.nr;
-      sm.col_t[par][lane] = live ? __ldg(g.row_token + s.row0 + lane) : 0;
+      const int t = live ? __ldg(g.row_token + s.row0 + lane) : 0;
+      const int k = live ? __ldg(g.row_nloc + s.row0 + lane) : 0;
       sm.col_w[par][lane] = live ? __ldg(g.row_weight + s.row0 + lane) : 0.f;
-      sm.col_k[par][lane] = live ? __ldg(g.row_nloc + s.row0 + lane) : 0;
+      sm.col_dst[par][lane] = k == 1 ? reinterpret_cast<uintptr_t>(out_row(g.out, t)) | 1u
+                                     : reinterpret_cast<uintptr_t>(g.part2 + static_cast<size_t>(s.row0 + lane) * kH);
     }
     named_bar_sync(1, kSEpiThreads);
     MOE_TADD(ts, t0);

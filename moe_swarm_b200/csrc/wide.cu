@@ -89,7 +89,10 @@ struct WideSmem {
   float amx[2][128];       // MODE 1: per-row amax of each column half
   // per-epilogue-warp staging of output rows so each warp store writes whole row segments
   alignas(16) uint8_t ostg[8][2560];
-  int mt[8][32];           // MODE 2: per-warp row metadata (output row or partial row)
+  // MODE 2: per-warp row destinations -- the row's bf16 output row (bit 0 set) for a token with one
+  // local expert, else its fp32 partial row -- resolved once per row, not at every store (the
+  // output map of expert parallelism divides and indexes per token)
+  uintptr_t mdst[8][32];
   int e_cnt[kEG + 1];
   int e_start[kEG + 1];
   int e_tiles[kEG + 1];
@@ -342,7 +345,8 @@ __device__ __forceinline__ void w_epi2(WideSmem<2>& sm, const TileArgs& g, const
   // staging [32 rows][16 floats]; the four 16-byte chunks of row r sit at chunk ^ ((r >> 1) & 3),
   // which makes both the row-wise vector stores and the column-chunk reads bank-conflict free
   float* st = reinterpret_cast<float*>(sm.ostg[ew]);
-  sm.mt[ew][lane] = kt == 1 ? -1 - t : t;              // < 0: the bf16 output row of token -1-v
+  sm.mdst[ew][lane] = kt == 1 ? reinterpret_cast<uintptr_t>(out_row(g.out, t)) | 1u
+                              : reinterpret_cast<uintptr_t>(g.part2 + static_cast<size_t>(s.row0 + 32 * q + lane) * kH);
   const int col0 = s.nt * 256 + 128 * h;
   const int swz = (lane >> 1) & 3;
   __syncwarp();
@@ -360,13 +364,13 @@ __device__ __forceinline__ void w_epi2(WideSmem<2>& sm, const TileArgs& g, const
       const int r = 8 * i + (lane >> 2), ch = lane & 3;
       if (r < rows_here) {
         const float4 v = *reinterpret_cast<const float4*>(st + r * 16 + 4 * (ch ^ ((r >> 1) & 3)));
-        const int tv = sm.mt[ew][r];
+        const uintptr_t d = sm.mdst[ew][r];
         const int col = col0 + 16 * rd + 4 * ch;
-        if (tv < 0) {
-          *reinterpret_cast<uint2*>(out_row(g.out, -1 - tv) + col) =
+        if (d & 1u) {
+          *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(d & ~uintptr_t(1)) + col) =
               make_uint2(bf16x2_bits(v.x, v.y), bf16x2_bits(v.z, v.w));
         } else {
-          *reinterpret_cast<float4*>(g.part2 + static_cast<size_t>(s.row0 + 32 * q + r) * kH + col) = v;
+          *reinterpret_cast<float4*>(reinterpret_cast<float*>(d) + col) = v;
         }
       }
     }
