@@ -107,7 +107,9 @@ typedef struct moe_b200_layout {
   size_t total;       /* bytes */
 } moe_b200_layout;
 
-/* Workspace bytes one call with this T and E_local needs (0 on bad arguments). */
+/* Workspace bytes one call with this T and E_local needs (0 on bad arguments).  Every entry point
+ * that takes a workspace requires it 256-byte aligned (cudaMalloc's alignment); others return
+ * MOE_B200_ERR_ARG. */
 MOE_B200_API size_t moe_b200_workspace_size(int32_t num_tokens, int32_t num_local_experts);
 
 /* Fills *out with the layout for (T, E_local).  Returns a status code. */

@@ -155,6 +155,8 @@ int prepare(const moe_b200_args* a, void* workspace, size_t ws_bytes, moe::Layou
     return fail(MOE_B200_ERR_ARG, "bad sizes");
   if (!workspace || ws_bytes < L->total)
     return fail(MOE_B200_ERR_WORKSPACE, "workspace too small: need " + std::to_string(L->total) + " bytes");
+  if (reinterpret_cast<uintptr_t>(workspace) & 255u)
+    return fail(MOE_B200_ERR_ARG, "workspace must be 256-byte aligned");
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
@@ -226,6 +228,7 @@ int moe_b200_workspace_init(void* workspace, size_t ws_bytes, int32_t num_tokens
   moe::Layout L;
   if (!moe::compute_layout(num_tokens, num_local_experts, &L)) return fail(MOE_B200_ERR_ARG, "bad sizes");
   if (!workspace || ws_bytes < L.total) return fail(MOE_B200_ERR_WORKSPACE, "workspace too small");
+  if (reinterpret_cast<uintptr_t>(workspace) & 255u) return fail(MOE_B200_ERR_ARG, "workspace must be 256-byte aligned");
   cudaError_t e = cudaMemsetAsync(static_cast<uint8_t*>(workspace) + L.counters_begin, 0,
                                   L.counters_end - L.counters_begin, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync");
@@ -310,6 +313,9 @@ int forward_impl(const moe_b200_args* a, void* workspace, size_t ws_bytes, void*
   } else {
     om.base[0] = a->output;
   }
+  om.al32 = 1;
+  for (int r = 0; r < moe::kMaxRanks; ++r)
+    if (om.base[r] && (reinterpret_cast<uintptr_t>(om.base[r]) & 31u)) om.al32 = 0;
   if (a->num_tokens == 0) return MOE_B200_OK;
   DeviceInfo& di = device_info(dev);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -512,6 +518,7 @@ int moe_b200_device_status(void* workspace, size_t ws_bytes, int32_t num_tokens,
   moe::Layout L;
   if (!moe::compute_layout(num_tokens, num_local_experts, &L)) return -fail(MOE_B200_ERR_ARG, "bad sizes");
   if (!workspace || ws_bytes < L.total) return -fail(MOE_B200_ERR_WORKSPACE, "workspace too small");
+  if (reinterpret_cast<uintptr_t>(workspace) & 255u) return -fail(MOE_B200_ERR_ARG, "workspace must be 256-byte aligned");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   int v = 0;
   int* p = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + L.status);

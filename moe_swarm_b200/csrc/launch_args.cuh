@@ -16,6 +16,7 @@ struct OutMap {
   uint16_t* base[kMaxRanks];   // [0]: the output; EP: each rank's receive buffer (this call's phase)
   int shard;                   // tokens per rank; 0: a single output
   int slot_rows;               // EP: this rank's slot, rank * shard rows into each receive buffer
+  int al32;                    // every base is 32-byte aligned (rows then are too: 14,336-byte pitch)
 };
 
 __host__ __device__ __forceinline__ uint16_t* out_row(const OutMap& m, int t) {

@@ -228,6 +228,18 @@ __device__ __forceinline__ uint64_t sdesc_k128_sw128(uint32_t smem_addr) {
   return d;
 }
 
+// 256-bit global stores (the address must be 32-byte aligned): one whole 32-byte sector per lane.
+__device__ __forceinline__ void st_global_v8(float* p, const float* v) {
+  asm volatile("st.global.v8.f32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};"
+               ::"l"(p), "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7])
+               : "memory");
+}
+__device__ __forceinline__ void st_global_v8_b32(void* p, const uint32_t* v) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};"
+               ::"l"(p), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
+}
+
 // ---------------------------------------------------------------- inter-CTA arrival
 // Arrival on a global counter with acquire-release semantics at GPU scope.  Used after a
 // CTA barrier by one thread, it publishes every store the CTA made before the barrier

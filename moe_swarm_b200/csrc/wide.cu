@@ -87,12 +87,8 @@ struct WideSmem {
   int flag;
   float ssw[2][kKB1];      // this segment's weight scales (MODE 1: X1, X2 blocks)
   float amx[2][128];       // MODE 1: per-row amax of each column half
-  // per-epilogue-warp staging of output rows so each warp store writes whole row segments
-  alignas(16) uint8_t ostg[8][2560];
-  // MODE 2: per-warp row destinations -- the row's bf16 output row (bit 0 set) for a token with one
-  // local expert, else its fp32 partial row -- resolved once per row, not at every store (the
-  // output map of expert parallelism divides and indexes per token)
-  uintptr_t mdst[8][32];
+  // MODE 1: per-epilogue-warp staging of output rows so each warp store writes whole row segments
+  alignas(16) uint8_t ostg[MODE == 1 ? 8 : 1][2560];
   int e_cnt[kEG + 1];
   int e_start[kEG + 1];
   int e_tiles[kEG + 1];
@@ -335,46 +331,47 @@ __device__ __forceinline__ void w_store1(WideSmem<1>& sm, const TileArgs& g, con
   }
 }
 
-// MODE 2 tile epilogue: this thread's 128 output columns of its token row: the bf16 output row
-// directly for a token with one local expert, otherwise the routing-weighted fp32 row for the
-// combine kernel.  Each warp writes its 32 rows x 128 columns in eight rounds of 16 columns
-// staged through shared memory, 8 whole 64-byte (fp32) row segments per store.
-__device__ __forceinline__ void w_epi2(WideSmem<2>& sm, const TileArgs& g, const WTile& s, const float* acc, int ew,
-                                       int h, int q, int lane, int t, float w, int kt) {
-  const int rows_here = min(32, s.nr - 32 * q);
-  // staging [32 rows][16 floats]; the four 16-byte chunks of row r sit at chunk ^ ((r >> 1) & 3),
-  // which makes both the row-wise vector stores and the column-chunk reads bank-conflict free
-  float* st = reinterpret_cast<float*>(sm.ostg[ew]);
-  sm.mdst[ew][lane] = kt == 1 ? reinterpret_cast<uintptr_t>(out_row(g.out, t)) | 1u
-                              : reinterpret_cast<uintptr_t>(g.part2 + static_cast<size_t>(s.row0 + 32 * q + lane) * kH);
+// MODE 2 tile epilogue: this thread's 128 output columns of its token row, stored straight from
+// registers: the bf16 output row for a token with one local expert, otherwise the
+// routing-weighted fp32 row for the combine kernel (combine.cu).  Each lane writes whole 32-byte
+// sectors of its own row (256-bit stores; bf16 rows with 128-bit stores when the output map is
+// only 16-byte aligned), so the epilogue uses no shared memory and no warp barriers while the
+// next tile's operands stream into the stages.
+__device__ __forceinline__ void w_epi2(const TileArgs& g, const WTile& s, const float* acc, int h, int rit, int t,
+                                       float w, int kt) {
+  if (rit >= s.nr) return;
   const int col0 = s.nt * 256 + 128 * h;
-  const int swz = (lane >> 1) & 3;
-  __syncwarp();
+  if (kt == 1) {
+    uint16_t* dst = out_row(g.out, t) + col0;
+    if (g.out.al32) {
 #pragma unroll
-  for (int rd = 0; rd < 8; ++rd) {
+      for (int i = 0; i < 8; ++i) {
+        uint32_t v[8];
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const float* a = acc + 16 * rd + 4 * c;
-      *reinterpret_cast<float4*>(st + lane * 16 + 4 * (c ^ swz)) =
-          make_float4(__fmul_rn(a[0], w), __fmul_rn(a[1], w), __fmul_rn(a[2], w), __fmul_rn(a[3], w));
-    }
-    __syncwarp();
+        for (int j = 0; j < 8; ++j)
+          v[j] = bf16x2_bits(__fmul_rn(acc[16 * i + 2 * j], w), __fmul_rn(acc[16 * i + 2 * j + 1], w));
+        st_global_v8_b32(dst + 16 * i, v);
+      }
+    } else {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int r = 8 * i + (lane >> 2), ch = lane & 3;
-      if (r < rows_here) {
-        const float4 v = *reinterpret_cast<const float4*>(st + r * 16 + 4 * (ch ^ ((r >> 1) & 3)));
-        const uintptr_t d = sm.mdst[ew][r];
-        const int col = col0 + 16 * rd + 4 * ch;
-        if (d & 1u) {
-          *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(d & ~uintptr_t(1)) + col) =
-              make_uint2(bf16x2_bits(v.x, v.y), bf16x2_bits(v.z, v.w));
-        } else {
-          *reinterpret_cast<float4*>(reinterpret_cast<float*>(d) + col) = v;
-        }
+      for (int i = 0; i < 16; ++i) {
+        uint4 v;
+        v.x = bf16x2_bits(__fmul_rn(acc[8 * i], w), __fmul_rn(acc[8 * i + 1], w));
+        v.y = bf16x2_bits(__fmul_rn(acc[8 * i + 2], w), __fmul_rn(acc[8 * i + 3], w));
+        v.z = bf16x2_bits(__fmul_rn(acc[8 * i + 4], w), __fmul_rn(acc[8 * i + 5], w));
+        v.w = bf16x2_bits(__fmul_rn(acc[8 * i + 6], w), __fmul_rn(acc[8 * i + 7], w));
+        *reinterpret_cast<uint4*>(dst + 8 * i) = v;
       }
     }
-    __syncwarp();
+  } else {
+    float* dst = g.part2 + static_cast<size_t>(s.row0 + rit) * kH + col0;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = __fmul_rn(acc[8 * i + j], w);
+      st_global_v8(dst + 8 * i, v);
+    }
   }
 }
 
@@ -577,7 +574,7 @@ __device__ __forceinline__ void w_epilogue(WideSmem<MODE>& sm, uint32_t tmem, co
       w_epi1(sm, g, s, acc1, acc2, h, rit, hw, lw);
       w_store1(sm, g, s, hw, lw, ew, q, h, lane);
     } else {
-      w_epi2(sm, g, s, acc1, ew, h, q, lane, meta_t, meta_w, meta_k);
+      w_epi2(g, s, acc1, h, rit, meta_t, meta_w, meta_k);
     }
     MOE_WADD(te, t0);
   }

@@ -72,6 +72,12 @@ def test_forward_rejects_bad_arguments_without_touching_a_gpu():
     a.gemm1_weights = (1 << 20) + 8
     assert lib.moe_b200_forward(ctypes.byref(a), None, 0, None) == N.ERR_ARG
     assert "aligned" in N.last_error()
+    # a large enough workspace that is not 256-byte aligned (rejected before any CUDA call)
+    a.gemm1_weights = 1 << 20
+    need = lib.moe_b200_workspace_size(4, 32)
+    assert lib.moe_b200_forward(ctypes.byref(a), ctypes.c_void_p((1 << 30) + 16), need, None) == N.ERR_ARG
+    assert "256-byte" in N.last_error()
+    assert lib.moe_b200_workspace_init(ctypes.c_void_p((1 << 30) + 16), need, 4, 32, None) == N.ERR_ARG
 
 
 def test_forward_ep_rejects_bad_arguments_without_touching_a_gpu():
