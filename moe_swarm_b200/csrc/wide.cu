@@ -87,8 +87,6 @@ struct WideSmem {
   int flag;
   float ssw[2][kKB1];      // this segment's weight scales (MODE 1: X1, X2 blocks)
   float amx[2][128];       // MODE 1: per-row amax of each column half
-  // MODE 1: per-epilogue-warp staging of output rows so each warp store writes whole row segments
-  alignas(16) uint8_t ostg[MODE == 1 ? 8 : 1][2560];
   int e_cnt[kEG + 1];
   int e_start[kEG + 1];
   int e_tiles[kEG + 1];
@@ -305,30 +303,16 @@ __device__ __forceinline__ void w_epi1(WideSmem<1>& sm, const TileArgs& g, const
     g.c_scale[static_cast<size_t>(s.nt) * g.r_pad + s.row0 + rit] = amax > 0.f ? amax / 448.0f : 1.0f;
 }
 
-// Stores this warp's 32 rows x 64 bytes (hi, then lo) through its staging buffer: each lane
-// stages its row, then every warp store writes 8 whole 64-byte row segments.
-__device__ __forceinline__ void w_store1(WideSmem<1>& sm, const TileArgs& g, const WTile& s, const uint32_t* hw,
-                                         const uint32_t* lw, int ew, int q, int h, int lane) {
-  uint8_t* st = sm.ostg[ew];
-  const int rows_here = min(32, s.nr - 32 * q);   // valid rows of this warp's quarter
-#pragma unroll
-  for (int part = 0; part < 2; ++part) {
-    const uint32_t* src = part == 0 ? hw : lw;
-    uint4* mine = reinterpret_cast<uint4*>(st + lane * 80);
-#pragma unroll
-    for (int v = 0; v < 4; ++v) mine[v] = make_uint4(src[4 * v], src[4 * v + 1], src[4 * v + 2], src[4 * v + 3]);
-    __syncwarp();
-    uint8_t* base = (part == 0 ? g.c_hi : g.c_lo) + static_cast<size_t>(s.row0 + 32 * q) * kI +
-                    static_cast<size_t>(s.nt) * kBlk + 64 * h;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int r = 8 * i + (lane >> 2), ch = lane & 3;
-      if (r < rows_here)
-        *reinterpret_cast<uint4*>(base + static_cast<size_t>(r) * kI + 16 * ch) =
-            *reinterpret_cast<const uint4*>(st + r * 80 + 16 * ch);
-    }
-    __syncwarp();
-  }
+// Stores this thread's 64 hi bytes and 64 lo bytes of its row (columns 64h.. of the tile's 128)
+// straight from registers: two 256-bit stores each, whole 32-byte sectors per lane.
+__device__ __forceinline__ void w_store1(const TileArgs& g, const WTile& s, const uint32_t* hw, const uint32_t* lw,
+                                         int h, int rit) {
+  if (rit >= s.nr) return;
+  const size_t off = static_cast<size_t>(s.row0 + rit) * kI + static_cast<size_t>(s.nt) * kBlk + 64 * h;
+  st_global_v8_b32(g.c_hi + off, hw);
+  st_global_v8_b32(g.c_hi + off + 32, hw + 8);
+  st_global_v8_b32(g.c_lo + off, lw);
+  st_global_v8_b32(g.c_lo + off + 32, lw + 8);
 }
 
 // MODE 2 tile epilogue: this thread's 128 output columns of its token row, stored straight from
@@ -572,7 +556,7 @@ __device__ __forceinline__ void w_epilogue(WideSmem<MODE>& sm, uint32_t tmem, co
     if constexpr (MODE == 1) {
       uint32_t hw[16], lw[16];
       w_epi1(sm, g, s, acc1, acc2, h, rit, hw, lw);
-      w_store1(sm, g, s, hw, lw, ew, q, h, lane);
+      w_store1(g, s, hw, lw, h, rit);
     } else {
       w_epi2(g, s, acc1, h, rit, meta_t, meta_w, meta_k);
     }
