@@ -192,7 +192,11 @@ class ClockSampler:
             return None
         sm = sorted(s[1] for s in inside)
         reasons = sorted({name for s in inside for bit, name in self.REASONS if s[2] & bit})
+        bits = 0
+        for s in inside:
+            bits |= s[2]
         return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "sm_mhz_range": [sm[0], sm[-1]], "reason_bits": hex(bits),
                 "samples": len(inside), "source": "nvml, 10 ms"}
 
 
