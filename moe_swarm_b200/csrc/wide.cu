@@ -16,9 +16,13 @@
 //     w * O goes to its fp32 partial row, summed in ascending expert order by the combine
 //     kernel (combine.cu).
 //
-// CTA = 12 warps: warp 0 TMA producer (one box per lane), warp 1 TMEM owner + single-thread MMA
+// CTA = 12 warps: warp 2 TMA producer (one box per lane), warp 3 TMEM owner + single-thread MMA
 // issuer (their warpgroup drops to 56 registers), warps 4..11 promotion/epilogue with 224
-// registers: two warps per TMEM lane quarter, one per 128-column half of the accumulator.
+// registers: two warps per TMEM lane quarter, one per 128-column half of the accumulator.  The
+// producer and the MMA issuer sit on the sub-partitions of lane quarters 2 and 3: the promotion
+// warps of a quarter that shares its sub-partition with them read the accumulator late (their
+// TMEM loads queue behind the issuers' instructions), and a partly filled token tile fills the
+// quarters from 0 upward, so its live quarters are the undisturbed ones.
 // Shared-memory stages: MODE 1 4 x 48 KB (128 token rows | 128 X1 rows | 128 X2 rows),
 // MODE 2 3 x 64 KB (128 hi rows | 128 lo rows | 256 W2 rows); 2 TMEM accumulator buffers of 256
 // columns.  Work: data-parallel
@@ -70,6 +74,8 @@ struct WCfg<2> {
   static constexpr int STAGE_BYTES = 4 * 16384;
 };
 constexpr int kWRows = 128;      // token rows per tile (MMA M)
+constexpr int kWProducerWarp = 2;   // sub-partition of lane quarter 2
+constexpr int kWMmaWarp = 3;        // sub-partition of lane quarter 3; also owns the TMEM allocation
 
 constexpr int kWThreads = 384;   // 3 warpgroups: producer/MMA (+2 idle warps), 2 x epilogue
 constexpr int kWEpiThreads = 256;
@@ -614,7 +620,7 @@ __global__ void __launch_bounds__(kWThreads, 1)
     tma_prefetch_desc(&tmA2);
     tma_prefetch_desc(&tmB);
   }
-  if (warp == 1) {
+  if (warp == kWMmaWarp) {
     tmem_alloc(&sm.tmem_base, 512);
     tmem_relinquish();
   }
@@ -631,9 +637,9 @@ __global__ void __launch_bounds__(kWThreads, 1)
   // 384 threads x 168 registers at launch = 128 x 56 (producer/MMA warpgroup) + 256 x 224
   if (warp < 4) {
     setmaxnreg_dec<56>();
-    if (warp == 0) {
+    if (warp == kWProducerWarp) {
       w_producer<MODE>(sm, &tmA, &tmA2, &tmB, g, sk, lane);
-    } else if (warp == 1) {
+    } else if (warp == kWMmaWarp) {
       if (lane == 0) w_mma<MODE>(sm, tmem, g, sk);
       __syncwarp();
     }
@@ -644,7 +650,7 @@ __global__ void __launch_bounds__(kWThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == kWMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
