@@ -49,6 +49,8 @@ def test_samples_inside_window_and_reason_names(monkeypatch):
     r = cs.stop()
     assert r["sm_mhz"] == 1850 and r["sm_max_mhz"] == 1965
     assert r["reasons"] == ["sw_power_cap"]
+    assert r["reason_bits"] == "0x5"           # every bit seen, named or not (gpu idle included)
+    assert r["sm_mhz_range"] == [1850, 1850]
     assert 3 <= r["samples"] <= 20   # 10 ms period over a 120 ms window, none outside it
     assert r["source"].startswith("nvml")
 
